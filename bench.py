@@ -1,0 +1,399 @@
+"""Benchmark: µs per fused MoE layer and achieved HBM GB/s (decode, bs=1).
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--config mixtral|deepseek|dbrx|tiny]
+                [--parallel tp|ep] [--impl ours|reference]
+
+One step = one MoE layer forward for one decode token (router -> top-K ->
+SwiGLU over the selected experts -> weighted combine; plus the hidden-sized
+all-reduce when N > 1).  The default workload is the Mixtral-shaped layer
+(H 4096, I 14336, E 8, top_k 2, bf16 weights, fp32 accumulation/output),
+tensor-parallel over N GPUs.  Inputs are synthetic and seeded; layers rotate
+so every step streams weights from HBM (each step reads more than L2 holds).
+
+Rank 0 prints one JSON line.  `value` is µs per layer (max over ranks, CUDA
+events on the launching stream); `e2e` is the same through the public API
+with the token copied in from pinned host memory and the output copied back
+every step; `roofline` relates the fused kernel's algorithmic bytes to the
+measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
+composition (restated in oracle/torch_composition.py) on a bounded sample.
+`--impl reference` times that CPU composition alone, as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "warp-route_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "µs per MoE layer & achieved HBM GB/s, Mixtral shape bs=1, at 1/2/4/8 B200"
+SHAPES = {"tiny": (8, 512, 1024, 2), "mixtral": (8, 4096, 14336, 2),
+          "deepseek": (64, 2048, 1408, 6), "dbrx": (16, 6144, 10752, 4)}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--config", default="mixtral", choices=sorted(SHAPES))
+    ap.add_argument("--parallel", default="tp", choices=["tp", "ep"])
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="budget of the bounded CPU-baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(workload: str):
+    """DRAM bytes per launch of the fused kernel from a committed ncu summary."""
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f).get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, busy_only=True):
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+        except Exception:
+            return out
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if sm:
+            out.update(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), samples=len(sm))
+        out["reasons"] = sorted(reasons)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+        return out
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and args.impl == "ours":
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# CPU composition (warp-route's own CPU path, restated in oracle/)
+# ---------------------------------------------------------------------------
+def cpu_composition_timing(x, gate_w, weight_buf, E, H, I, K, budget_s, max_calls=None,
+                           bias=None):
+    """Time the restated torch_moe_reference on host threads.  Weights are the
+    same layer's selected experts, widened to fp32 (warp-route's own dtype)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import torch_composition as tc
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    xh = x.detach().float().cpu()
+    gwh = gate_w.detach().float().cpu()
+    bh = None if bias is None else bias.detach().float().cpu()
+    probs = torch.softmax(gwh @ xh + (bh if bh is not None else 0), dim=0)
+    sel = torch.topk(probs, K).indices.tolist()
+    elt = weight_buf.element_size()
+    stride = ((3 * H * I * elt + 127) // 128 * 128) // elt
+    n = I * H
+    gate, up, down = [None] * E, [None] * E, [None] * E
+    for e in sel:
+        blk = weight_buf[e * stride:e * stride + 3 * n].float().cpu()
+        gate[e] = blk[:n].view(I, H)
+        up[e] = blk[n:2 * n].view(I, H)
+        down[e] = blk[2 * n:].view(H, I)
+    for _ in range(3):
+        tc.moe_forward(xh, gwh, gate, up, down, K, bh)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end and (max_calls is None or len(times) < max_calls):
+        t0 = time.perf_counter()
+        tc.moe_forward(xh, gwh, gate, up, down, K, bh)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, len(times), threads
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    from warp_route import synthetic
+
+    E, H, I, K = SHAPES[args.config]
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    L = synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=0)
+    budget = min(60.0, max(5.0, args.cpu_seconds))
+    us, n, cores = cpu_composition_timing(L.x, L.gate_w, L.weight_buf, E, H, I, K, budget,
+                                          max_calls=args.steps)
+    sample = (f"{n} forwards of the {args.config} layer (bs=1, fp32 weights of the selected "
+              f"experts), median; warp-route's torch composition restated")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": n, "warmup": 3, "ms_per_step": round(us / 1000, 4),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config}_bs1", "E": E, "H": H, "I": I, "top_k": K,
+                   "tokens": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(us, 2), "unit": "us/layer", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(us, 2), "unit": "us/layer", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import torch.distributed as dist
+
+    from warp_route import functional as F
+    from warp_route import synthetic
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    E, H, I, K = SHAPES[args.config]
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    elt = 2 if dt == torch.bfloat16 else 4
+    tp = world if args.parallel == "tp" and world > 1 else 1
+    ep = world if args.parallel == "ep" and world > 1 else 1
+    # Rotate enough layers that the bytes streamed between two reads of the
+    # same layer exceed 4x L2 (cold HBM every step).
+    sel_bytes = K * 3 * H * (I // tp) * elt
+    n_layers = max(2, math.ceil(4 * L2_BYTES / max(1, sel_bytes)) + 1)
+    layer_bytes = E // ep * 3 * H * (I // tp) * elt
+    n_layers = min(n_layers, max(2, int(100e9 // layer_bytes)))
+    layers = []
+    for li in range(n_layers):
+        layers.append(synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100 + li,
+                                           layer=li, tp_rank=rank if tp > 1 else 0, tp_size=tp,
+                                           ep_rank=rank if ep > 1 else 0, ep_size=ep))
+    Il = I // tp
+
+    # routing of each layer (identical on all ranks) -> algorithmic bytes
+    distinct = []
+    for Lr in layers:
+        _, ids, _ = F.fused_moe_routed(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
+                                       ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)
+        sel = set(ids.cpu().view(-1).tolist())
+        if ep > 1:
+            sel = {e for e in sel if Lr.ep_first <= e < Lr.ep_first + Lr.ep_num}
+        distinct.append(len(sel))
+    bytes_per_layer = [synthetic.algorithmic_bytes(E, H, Il, u, 1, elt) for u in distinct]
+    avg_bytes = sum(bytes_per_layer) / len(bytes_per_layer)
+
+    def layer_call(Lr):
+        if ep > 1:
+            return F.fused_moe_routed(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
+                                      ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)[0]
+        return F.fused_moe(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K)
+
+    stream = torch.cuda.current_stream()
+    W, Ksteps = args.warmup, args.steps
+    for i in range(W):
+        out = layer_call(layers[i % n_layers])
+        if world > 1:
+            dist.all_reduce(out)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing ----
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for i in range(Ksteps):
+            k_start[i].record(stream)
+            out = layer_call(layers[i % n_layers])
+            k_end[i].record(stream)
+            if world > 1:
+                dist.all_reduce(out)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clk.summary()
+    total_ms = t0.elapsed_time(t1)
+    kern_ms = [a.elapsed_time(b) for a, b in zip(k_start, k_end)]
+    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    t = torch.tensor([total_ms, kern_avg_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, kern_avg_ms = t.tolist()
+    us_per_layer = total_ms * 1000.0 / Ksteps
+
+    # ---- end-to-end through the public API, host buffers in and out ----
+    Ke = Ksteps
+    x_host = [torch.empty(H, dtype=dt).pin_memory() for _ in range(n_layers)]
+    for li, Lr in enumerate(layers):
+        x_host[li].copy_(Lr.x.cpu())
+    y_host = torch.empty(Ke if Ke <= 4096 else 4096, H, dtype=torch.float32).pin_memory()
+    x_dev = [torch.empty(H, dtype=dt, device=dev) for _ in range(n_layers)]
+    for i in range(min(W, 8)):
+        Lr = layers[i % n_layers]
+        x_dev[i % n_layers].copy_(x_host[i % n_layers], non_blocking=True)
+        o = F.fused_moe(x_dev[i % n_layers], Lr.gate_w, Lr.weight_buf, E, H, Il, K) if ep == 1 \
+            else layer_call(Lr)
+        if world > 1:
+            dist.all_reduce(o)
+        y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(Ke):
+        li = i % n_layers
+        Lr = layers[li]
+        x_dev[li].copy_(x_host[li], non_blocking=True)
+        if ep == 1:
+            o = F.fused_moe(x_dev[li], Lr.gate_w, Lr.weight_buf, E, H, Il, K)
+        else:
+            o = F.fused_moe_routed(x_dev[li], Lr.gate_w, Lr.weight_buf, E, H, Il, K,
+                                   ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)[0]
+        if world > 1:
+            dist.all_reduce(o)
+        y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_us = te.item() * 1000.0 / Ke
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        full = layers[0]
+        us_cpu, ncalls, cores = cpu_composition_timing(full.x, full.gate_w, full.weight_buf, E, H,
+                                                       Il, K, args.cpu_seconds)
+        cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
+               "sample": f"{ncalls} single-token forwards of layer 0 ({args.config}), the "
+                         f"selected experts widened to fp32, median of {ncalls} after 3 warm-ups; "
+                         f"warp-route's torch composition restated in oracle/torch_composition.py"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        peak, peak_kind = peaks()
+        # the fused kernel's bytes per launch on the busiest rank (identical per rank for TP)
+        achieved = avg_bytes / (kern_avg_ms * 1e-3) / 1e9
+        workload = f"{args.config}_bs1_{args.dtype}" + (f"_{args.parallel}{world}" if world > 1 else "")
+        traffic = ncu_traffic(workload)
+        line = {
+            "metric": METRIC, "value": round(us_per_layer, 3), "unit": "us/layer",
+            "n_gpus": world, "steps": Ksteps, "warmup": W,
+            "ms_per_step": round(total_ms / Ksteps, 6), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+            "config": {"workload": workload, "E": E, "H": H, "I": I, "top_k": K, "tokens": 1,
+                       "parallelism": f"{args.parallel}{world}" if world > 1 else "single",
+                       "l2": f"inputs larger than L2: {n_layers} rotating layers, "
+                             f"{avg_bytes / 1e6:.1f} MB streamed per step",
+                       "layers_rotated": n_layers},
+            "hbm_gbs": round(avg_bytes / (us_per_layer * 1e-6) / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind,
+                         "traffic": traffic,
+                         "kernel_us": round(kern_avg_ms * 1000, 3),
+                         "algorithmic_bytes": int(avg_bytes)},
+            "e2e": {"value": round(e2e_us, 3), "unit": "us/layer",
+                    "h2d_bytes_per_step": H * elt * world,
+                    "d2h_bytes_per_step": H * 4 * world},
+            "gpu_launches": Ksteps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+    run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,186 @@
+/*
+ * warp_route_b200.h — C ABI of the B200-native fused decode-time MoE layer.
+ *
+ * Plain pointers and sizes only: no torch, no C++ types.  Every entry point
+ * returns a wr_status_t and never calls exit(); every launch goes on the
+ * stream the caller passes, and no entry point blocks the host or allocates
+ * device memory unless its comment says so.  The caller owns every buffer.
+ *
+ * Each declaration names the warp-route interface it replaces, as
+ * path:line within the warp-route project (anishesg/warp-route).
+ *
+ * Arithmetic contract (shared by all compute entry points; follows
+ * src/fused_moe.cu:100-226 and tests/test_python.py:15-37):
+ *   logits[e] = gate_w[e,:] . x   (+ router_bias[e] when given), fp32;
+ *   probs     = softmax(logits) over all E experts, fp32;
+ *   top-K     = iterative argmax over the logits with strict '>', so ties go
+ *               to the lowest expert index; weight_k = probs[id_k] (NOT
+ *               renormalised over the K selected experts);
+ *   out       = sum_k weight_k * Wd_k (silu(Wg_k x) * (Wu_k x)),
+ *               silu(g) = g / (1 + exp(-g)); accumulated and returned in fp32.
+ * The logits are computed in fp32 with one fixed reduction order (a 32-lane
+ * strided fma sweep over 16-byte vectors, then a 16/8/4/2/1 xor tree), so the
+ * selected expert indices are reproducible bit for bit on any device and by
+ * the CPU oracle.
+ */
+#ifndef WARP_ROUTE_B200_H
+#define WARP_ROUTE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WR_API __attribute__((visibility("default")))
+#else
+#define WR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle: a cudaStream_t passed through unchanged (NULL = the
+ * legacy default stream, as in the warp-route launchers). */
+typedef void* wr_stream_t;
+
+typedef enum wr_status {
+  WR_OK = 0,
+  WR_ERR_INVALID = 1,      /* bad argument: null pointer, shape, top_k, ... */
+  WR_ERR_UNSUPPORTED = 2,  /* valid in warp-route but outside this build's limits */
+  WR_ERR_CUDA = 3,         /* a CUDA runtime call failed (see wr_last_error_string) */
+  WR_ERR_TIMEOUT = 4,      /* a bounded device-side wait gave up */
+  WR_ERR_WORKSPACE = 5,    /* workspace missing, misaligned or too small */
+  WR_ERR_TOO_SMALL = 6,    /* weight_buf smaller than the layout requires */
+  WR_ERR_COMM = 7          /* multi-GPU communicator error */
+} wr_status_t;
+
+typedef enum wr_dtype {
+  WR_DTYPE_F32 = 0,   /* float32 x / gate_w / weight_buf (warp-route's only dtype) */
+  WR_DTYPE_BF16 = 1   /* bfloat16 x / gate_w / weight_buf, fp32 accumulation and output */
+} wr_dtype_t;
+
+/* Shape of one MoE layer.  Replaces ExpertLayoutConfig + top_k
+ * (src/expert_layout.cuh:20-24, src/fused_moe.cuh:17-22).
+ * ep_first_expert / ep_num_local describe an expert-parallel shard: the
+ * weight_buf then holds experts [ep_first_expert, ep_first_expert +
+ * ep_num_local) packed from slot 0, the router still scores all num_experts
+ * experts, and selected experts outside the shard contribute zero.
+ * ep_num_local = 0 means every expert is local (no expert parallelism). */
+typedef struct wr_moe_desc {
+  int32_t num_experts;
+  int32_t hidden_dim;
+  int32_t intermediate_dim;
+  int32_t top_k;
+  int32_t dtype;            /* wr_dtype_t */
+  int32_t ep_first_expert;
+  int32_t ep_num_local;
+  int32_t reserved;
+  const float* router_bias; /* optional fp32 [num_experts] added to the logits; NULL = none */
+} wr_moe_desc_t;
+
+/* Byte offsets inside one packed expert block.  Replaces ExpertOffsets
+ * (src/expert_layout.cuh:27-32). */
+typedef struct wr_expert_offsets {
+  int64_t gate_proj_offset;
+  int64_t up_proj_offset;
+  int64_t down_proj_offset;
+  int64_t expert_stride;    /* 128-byte aligned */
+} wr_expert_offsets_t;
+
+/* ---- layout ------------------------------------------------------------ */
+
+/* Per-expert [gate I x H | up I x H | down H x I] row-major offsets for an
+ * element size of elt_bytes (4 reproduces warp-route's float layout byte for
+ * byte).  Replaces compute_offsets (src/expert_layout.cuh:34-47). */
+WR_API wr_status_t wr_expert_offsets(int32_t hidden_dim, int32_t intermediate_dim,
+                              int32_t elt_bytes, wr_expert_offsets_t* out);
+
+/* Bytes of a packed buffer of num_experts experts.  Replaces
+ * total_weight_bytes (src/expert_layout.cuh:74-77). */
+WR_API int64_t wr_total_weight_bytes(int32_t num_experts, int32_t hidden_dim,
+                              int32_t intermediate_dim, int32_t elt_bytes);
+
+/* ---- status ------------------------------------------------------------ */
+
+WR_API const char* wr_status_string(wr_status_t s);
+/* Text of the most recent error raised on the calling thread (argument
+ * checks name the argument, as the TORCH_CHECK messages of
+ * src/bindings.cpp:9-23,40-43,75-83 do). */
+WR_API const char* wr_last_error_string(void);
+/* Library version string. */
+WR_API const char* wr_version(void);
+
+/* ---- router ------------------------------------------------------------ */
+
+/* Router + softmax + top-K for num_tokens tokens (x: [num_tokens, H]).
+ * Writes fp32 logits [T,E] (optional, may be NULL), int32 ids [T,K] and fp32
+ * weights [T,K].  Replaces warp_gate_topk (src/gate.cu:103-116, declared
+ * src/gate.cuh:24-30) and the inlined router of src/fused_moe.cu:100-150. */
+WR_API wr_status_t wr_router_topk(const wr_moe_desc_t* desc, int32_t num_tokens,
+                           const void* x, const void* gate_w,
+                           float* logits_out, int32_t* topk_ids,
+                           float* topk_weights, wr_stream_t stream);
+
+/* ---- fused layer, one token ------------------------------------------- */
+
+/* Device workspace the fused single-token and batched entry points need for
+ * num_tokens tokens (bytes, 256-byte aligned base required).  The workspace
+ * must be zero-filled before its first use; every call leaves it reusable.
+ * Calls that share one workspace must not overlap on the GPU. */
+WR_API size_t wr_fused_moe_workspace_size(const wr_moe_desc_t* desc, int32_t num_tokens);
+
+/* One decode token: x [H] -> out [H] (fp32).  topk_ids [K] / topk_weights [K]
+ * are optional (NULL to skip).  Replaces fused_moe_forward
+ * (src/fused_moe.cu:233-263, declared src/fused_moe.cuh:28-32) and the
+ * binding fused_moe_forward_torch (src/bindings.cpp:62-97). */
+WR_API wr_status_t wr_fused_moe(const wr_moe_desc_t* desc, const void* x,
+                         const void* gate_w, const void* weight_buf,
+                         int64_t weight_buf_bytes, float* out,
+                         int32_t* topk_ids, float* topk_weights,
+                         void* workspace, size_t workspace_bytes,
+                         wr_stream_t stream);
+
+/* ---- fused layer, a batch of tokens ----------------------------------- */
+
+/* num_tokens decode tokens: x [T,H] -> out [T,H] (fp32); topk_ids [T,K] and
+ * topk_weights [T,K] optional.  Replaces batched_fused_moe_forward
+ * (src/fused_moe_batched.cu:186-214, declared src/fused_moe_batched.cuh:29-33)
+ * and batched_fused_moe_forward_torch (src/bindings.cpp:101-143). */
+WR_API wr_status_t wr_batched_fused_moe(const wr_moe_desc_t* desc, int32_t num_tokens,
+                                 const void* x, const void* gate_w,
+                                 const void* weight_buf, int64_t weight_buf_bytes,
+                                 float* out, int32_t* topk_ids,
+                                 float* topk_weights, void* workspace,
+                                 size_t workspace_bytes, wr_stream_t stream);
+
+/* ---- naive multi-kernel layer ----------------------------------------- */
+
+/* Scratch bytes for wr_naive_moe.  Replaces naive_moe_alloc_scratch /
+ * NaiveMoEScratch (src/naive_moe.cu:24-33, src/naive_moe.cuh:25-32); the
+ * caller allocates, so the call itself allocates nothing. */
+WR_API size_t wr_naive_moe_workspace_size(const wr_moe_desc_t* desc);
+
+/* Unfused layer, one kernel per step (router, top-K, gate, up, SwiGLU, down,
+ * weighted accumulate).  Top-K runs on the device, so unlike warp-route there
+ * is no mid-forward host synchronisation.  Replaces naive_moe_forward
+ * (src/naive_moe.cu:181-241, declared src/naive_moe.cuh:39-44) and
+ * naive_moe_forward_torch (src/bindings.cpp:26-59). */
+WR_API wr_status_t wr_naive_moe(const wr_moe_desc_t* desc, const void* x,
+                         const void* gate_w, const void* weight_buf,
+                         int64_t weight_buf_bytes, float* out,
+                         void* workspace, size_t workspace_bytes,
+                         wr_stream_t stream);
+
+/* ---- device status ----------------------------------------------------- */
+
+/* Reads (and clears) the status word a fused call left in its workspace:
+ * WR_OK, or WR_ERR_TIMEOUT when a bounded wait inside a kernel gave up.
+ * Synchronises `stream`.  No warp-route counterpart (warp-route kernels have
+ * no bounded waits). */
+WR_API wr_status_t wr_workspace_status(void* workspace, wr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WARP_ROUTE_B200_H */

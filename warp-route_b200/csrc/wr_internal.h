@@ -1,0 +1,48 @@
+// wr_internal.h — host-side declarations shared by the C ABI (wr_api.cu) and
+// the kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/warp_route_b200.h"
+
+namespace wr {
+
+// Per-call problem description after validation.
+struct Problem {
+  int E, H, I, K, T;          // experts, hidden, intermediate, top_k, tokens
+  int ep_first, ep_num;       // expert-parallel shard (ep_num = E: no EP)
+  int dtype;                  // wr_dtype_t
+  int elt;                    // bytes per element
+  const float* router_bias;   // optional [E]
+};
+
+// Sets the thread's last-error text (printf-style) and returns `s`.
+wr_status_t fail(wr_status_t s, const char* fmt, ...);
+
+// Maps a CUDA error to WR_ERR_CUDA with a message naming `what`.
+wr_status_t cuda_fail(cudaError_t e, const char* what);
+
+// ---- fused streaming kernel (wr_fused.cu) ----
+// True when the streaming kernel can take this problem (alignment, sizes).
+bool fused_supported(const Problem& p);
+size_t fused_workspace_bytes(const Problem& p);
+wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
+                         const void* wbuf, float* out, int32_t* ids, float* w,
+                         void* ws, cudaStream_t stream);
+
+// ---- router kernel (wr_naive.cu) ----
+wr_status_t launch_router(const Problem& p, const void* x, const void* gate_w,
+                          float* logits, int32_t* ids, float* w, cudaStream_t stream);
+
+// ---- naive multi-kernel path (wr_naive.cu) ----
+size_t naive_workspace_bytes(const Problem& p);
+wr_status_t launch_naive(const Problem& p, const void* x, const void* gate_w,
+                         const void* wbuf, float* out, int32_t* ids, float* w,
+                         void* ws, cudaStream_t stream);
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+}  // namespace wr
