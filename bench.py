@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of the bounded CPU-baseline sample")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="rotating layers (0: enough to exceed 4x L2 between reuses)")
     return ap.parse_args()
 
 
@@ -236,6 +238,8 @@ def run_ours(args, world, rank, local):
     n_layers = max(2, math.ceil(4 * L2_BYTES / max(1, sel_bytes)) + 1)
     layer_bytes = E // ep * 3 * H * (I // tp) * elt
     n_layers = min(n_layers, max(2, int(100e9 // layer_bytes)))
+    if args.layers > 0:
+        n_layers = args.layers
     layers = []
     for li in range(n_layers):
         layers.append(synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100 + li,
@@ -336,6 +340,10 @@ def run_ours(args, world, rank, local):
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_us = te.item() * 1000.0 / Ke
+    # A bounded device wait that gave up would make the timings meaningless.
+    status = F._load_extension().workspace_status(layers[0].x)
+    if status != 0:
+        raise SystemExit(f"fused kernel reported device status {status}: timing discarded")
 
     # ---- CPU baseline (rank 0, N = 1 only) ----
     cpu = None

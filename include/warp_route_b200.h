@@ -18,8 +18,9 @@
  *               renormalised over the K selected experts);
  *   out       = sum_k weight_k * Wd_k (silu(Wg_k x) * (Wu_k x)),
  *               silu(g) = g / (1 + exp(-g)); accumulated and returned in fp32.
- * The logits are computed in fp32 with one fixed reduction order (a 32-lane
- * strided fma sweep over 16-byte vectors, then a 16/8/4/2/1 xor tree), so the
+ * The logits are computed in fp32 with one fixed reduction order (the row's
+ * 16-byte vectors cut into 8 segments; per segment a 32-lane strided fma
+ * sweep and a 16/8/4/2/1 xor tree; segment sums added left to right), so the
  * selected expert indices are reproducible bit for bit on any device and by
  * the CPU oracle.
  */

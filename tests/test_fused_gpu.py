@@ -93,8 +93,9 @@ def test_token_batches(T, dtype):
     (64, 256, 256, 6, torch.bfloat16),     # many small experts
     (5, 100, 52, 2, torch.float32),        # ragged shapes -> unaligned path
     (6, 200, 36, 3, torch.bfloat16),       # ragged bf16 (H % 8 != 0)
-    (8, 23808, 256, 2, torch.bfloat16),    # largest H the streaming kernel keeps in smem
-    (8, 23816, 256, 2, torch.bfloat16),    # one vector more: unaligned/naive path
+    (8, 21248, 256, 2, torch.bfloat16),    # largest H the streaming kernel keeps in smem
+    (8, 21256, 256, 2, torch.bfloat16),    # one vector more: the naive path takes it
+    (8, 8200, 512, 2, torch.bfloat16),     # gate/up rows split across stages
 ])
 def test_edge_shapes(E, H, I, K, dtype):
     L = synthetic.make_layer(E, H, I, K, dtype=dtype, seed=5)

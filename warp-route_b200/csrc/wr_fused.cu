@@ -4,26 +4,45 @@
 // Replaces warp-route's k_fused_moe / k_fused_moe_batched
 // (src/fused_moe.cu:76-227, src/fused_moe_batched.cu:66-180): the same
 // router -> top-K -> SwiGLU over the selected experts -> weighted combine,
-// but spread over every SM instead of one warp.
+// spread over every SM instead of one warp.
 //
-// One persistent CTA per SM (cooperative launch, 227 KB of shared memory):
-//   warps 0-7  consumers: router, then dot products out of shared memory;
-//   warp 8     producer: one elected lane issues cp.async.bulk copies of
-//              weight rows into a 4-stage ring (mbarrier full/empty pairs),
-//              L2 evict-first, never waiting on the math.
-// Every CTA computes the router redundantly (the router rows are L2
-// resident), so all CTAs agree on the selection without a grid sync.
-// The selected experts become "slots"; the layer is then two matvecs over
-// virtual matrices built from the slots' packed blocks:
-//   phase A  rows p = slot*I + i of [Wg; Wu] . x  ->  act[p] =
-//            w_slot * silu(g) * u        (fp32, workspace, per token)
-//   phase B  out[h] = sum_c Wd_virtual[h, c] * act[c],  c over slot*I + i
-// Phase A rows and phase B rows are split evenly over the CTAs.  Between
-// the phases one grid-wide barrier (bounded spin) makes act visible; the
-// producer keeps streaming phase-B weights across it, so HBM never idles.
-// Phase B reads act through shared memory in windows of up to ~93 KB.
-// Results are deterministic: fixed lane order, fixed xor trees, fixed
-// window order, no floating-point atomics.
+// Two kernels per layer on one stream:
+//   k_router_logits  one CTA per (8 experts, token): every logit computed
+//                    once, written to the workspace.  It triggers the
+//                    dependent launch at once, so
+//   k_fused_stream   (programmatic dependent launch) is already resident,
+//                    has its barriers set up and x in shared memory, when
+//                    griddepcontrol.wait releases it.
+// k_fused_stream: one persistent CTA per SM (227 KB shared memory):
+//   warps 0-7  consumers: selection, then dot products out of shared memory;
+//   warp 8     producer: lane 0 issues cp.async.bulk copies into a ring of
+//              7-12 stages of ~16 KB (mbarrier full/empty pairs, L2
+//              evict-first) and never waits on the math.
+// Every copy is a contiguous run of weight rows (8-32 KB): B200's TMA
+// streams at HBM bandwidth only with large contiguous copies.
+//
+// The selected experts become "slots"; the layer is then two matvecs:
+//   phase A  rows p = slot*I + i of [Wg; Wu] . x -> act[p] =
+//            w_slot * silu(g) * u (fp32 workspace, one value per token).
+//            A stage holds GA gate rows and the same GA up rows (two copies).
+//   phase B  out[h] = sum over slots of Wd_slot[h, :] . act[slot, :].  The
+//            slot's activations sit in shared memory in windows of at most
+//            16 KB of weight columns; a stage is GB rows of one window.
+// Each row is owned by one warp (row index mod 8) that computes its whole
+// dot product.  Only the owners of a stage wait for it, process it and
+// release it (the producer pre-arrives for the others), so the eight warps
+// work on eight different stages at once.  Because a warp skips the stages
+// it does not own, a parity wait alone could mistake a later use of the
+// ring slot for the one it wants; the producer therefore tags each slot
+// with the number of the stage it holds, and an owner waits for its tag
+// before its parity wait (the tag is written only after the slot's previous
+// use was released, so the parity is then unambiguous).  No partial sum crosses a
+// warp, so results are deterministic (fixed lane order and trees, fixed
+// slot/window order, no floating-point atomics).  Phase A rows and phase B
+// rows are split evenly over the CTAs, each CTA starting at a rotated
+// position of its range (spreads DRAM channels).  One grid-wide barrier
+// (bounded spin) separates the phases; the producer keeps prefetching
+// phase-B weights across it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -38,71 +57,273 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;  // + producer warp
-constexpr int kStageBytes = 32 * 1024;
-constexpr int kStages = 4;
-constexpr int kRingBytes = kStages * kStageBytes;
+constexpr int kTargetStage = 16 * 1024;          // stage size aimed for
+constexpr int kMaxStageBytes = 32 * 1024;
+constexpr int kMaxStages = 12;
 constexpr int kSmemBytes = 232448;  // 227 KB: the sm_100 per-CTA opt-in maximum
-constexpr int kMiscBytes = 6144;
-constexpr int kVecBytes = kSmemBytes - kRingBytes - kMiscBytes;  // x / act window
+constexpr int kMiscBytes = 8192;
+constexpr int kMiscOff = kSmemBytes - kMiscBytes;
 constexpr int kMaxNT = 4;
-static_assert(kVecBytes % 16 == 0, "vector region must keep 16-byte alignment");
+constexpr int kMaxRowsPerStage = 32;
+constexpr int kRowsPerWarp = kMaxRowsPerStage / kConsumerWarps;  // owned rows per warp per stage
+// Room for at least 4 of the largest stages.
+constexpr int kVecMaxBytes = kMiscOff - 4 * kMaxStageBytes;  // x / activation window
+static_assert(kVecMaxBytes % 64 == 0, "vector region must keep 64-byte alignment");
 
-// Offsets inside the misc region.
-constexpr int kOffBars = 0;        // full[kStages], empty[kStages], act
-constexpr int kOffAbort = 128;     // int
-constexpr int kOffNSlots = 132;    // int
-constexpr int kOffSlotE = 256;     // int [64]: local expert of each slot
-constexpr int kOffSlotW = 512;     // float [64 * NT]: routing weight (0: not routed)
-constexpr int kOffLogits = 1536;   // float [NT * 64]
-constexpr int kOffTokIds = 2560;   // int [NT * 64]
-constexpr int kOffTokW = 3584;     // float [NT * 64]
-static_assert(kOffTokW + 4 * kMaxNT * kMaxExperts <= kMiscBytes, "misc region overflow");
+// Offsets inside the misc region (at the end of shared memory).
+constexpr int kOffBars = 0;        // full[12], empty[12], act
+constexpr int kOffAbort = 256;     // int
+constexpr int kOffNSlots = 260;    // int
+constexpr int kOffSlotTag = 264;   // int [12]: stage number each ring slot currently holds
+constexpr int kOffSlotE = 512;     // int [64]: local expert of each slot
+constexpr int kOffSlotW = 768;     // float [64 * NT]: routing weight (0: not routed)
+constexpr int kOffTokIds = 1792;   // int [NT * 64]
+constexpr int kOffTokW = 2816;     // float [NT * 64]
+constexpr int kOffRowAcc = 3840;   // float [rows * NT]: phase-B row accumulators
+constexpr int kRowAccFloats = (kMiscBytes - kOffRowAcc) / 4;
+static_assert(kOffBars + 8 * (2 * kMaxStages + 1) <= kOffAbort, "misc");
+static_assert(kRowAccFloats >= 1024, "misc");
 
-// Workspace words (uint32) in front of the activation buffer.
+// Workspace: control words, router logits, activations.
 constexpr int kSyncArrive = 0;
 constexpr int kSyncExit = 1;
 constexpr int kSyncStatus = 2;
 constexpr size_t kSyncBytes = 256;
+constexpr size_t kLogitBytes = (size_t)kMaxNT * kMaxExperts * 4;  // 1 KB
+constexpr size_t kActOffset = kSyncBytes + kLogitBytes;
+
+// Named barrier 1: the eight consumer warps.
+constexpr int kBarConsumers = 1;
+
+// Stage geometry, computed once on the host.
+struct Plan {
+  int GA;    // phase A: row pairs per stage
+  int CWA;   // phase A: columns per stage (H when whole rows fit)
+  int WB;    // phase B: activation window width (columns of one slot)
+  int nwin;  // phase B: windows per slot
+  int GB;    // phase B: rows per stage
+  int SB;    // stage bytes
+  int nst;   // ring stages
+};
 
 struct FusedArgs {
   const void* x;
-  const void* gate_w;
-  const float* router_bias;
   const uint8_t* wbuf;
   float* out;
   int32_t* ids_out;
   float* w_out;
+  const float* logits;  // [T][E] from k_router_logits
   float* act;
   uint32_t* sync;
   int E, H, I, K, T;
   int ep_first, ep_num;
   Layout lay;
+  Plan pl;
 };
 
-// Balanced split of n items into parts: [n*i/parts, n*(i+1)/parts).
-WR_DEVINL int split_lo(int64_t n, int i, int parts) { return (int)((n * i) / parts); }
+WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts; }
+
+WR_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+WR_DEVINL void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Router logits: grid (ceil(E/8), T), 256 threads.  Warp j computes segment j
+// of 8 router rows; the 8 segment sums are added in order (the order of
+// wr_router.cuh, shared with k_router and the CPU oracle).
+// ---------------------------------------------------------------------------
+template <typename Tw>
+__global__ void __launch_bounds__(kConsumerThreads) k_router_logits(const Tw* __restrict__ x,
+                                                                    const Tw* __restrict__ gate_w,
+                                                                    const float* __restrict__ bias,
+                                                                    int E, int H,
+                                                                    float* __restrict__ logits) {
+  griddep_launch_dependents();
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float parts[kRouterSegments * 8];
+  const int t = blockIdx.y;
+  const int e0 = blockIdx.x * 8;
+  const int nr = min(8, E - e0);
+  constexpr int VEC = Chunk<Tw>::kVec;
+  const Tw* xt = x + (int64_t)t * H;
+  for (int v = threadIdx.x; v < H / VEC; v += blockDim.x) {
+    float f[VEC];
+    Chunk<Tw>::widen(ldg_nc_v4(xt + (int64_t)v * VEC), f);
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) xs[v * VEC + q] = f[q];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  router_segment_warp<Tw>(gate_w + (int64_t)e0 * H, xs, nr, H, warp, lane, true,
+                          parts + warp * 8);
+  __syncthreads();
+  if (threadIdx.x < nr) {
+    const int r = threadIdx.x;
+    float l = parts[r];
+#pragma unroll
+    for (int j = 1; j < kRouterSegments; ++j) l = __fadd_rn(l, parts[j * 8 + r]);
+    if (bias) l = __fadd_rn(l, bias[e0 + r]);
+    logits[(int64_t)t * E + e0 + r] = l;
+  }
+}
+
+// Phase A dot products of one gate row and one up row over chunks [j0, j1)
+// (16-byte chunks of VEC elements starting at column c0) against x.
+template <typename Tw, int NT>
+WR_DEVINL void dot_pair(const uint4* __restrict__ gp, const uint4* __restrict__ up,
+                        const float* __restrict__ xs, int H, int c0, int j0, int j1, int lane,
+                        float (&g)[NT], float (&u)[NT]) {
+  constexpr int VEC = Chunk<Tw>::kVec;
+  float g1[NT], u1[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) g1[t] = u1[t] = 0.0f;
+#pragma unroll 4
+  for (int j = j0 + lane; j < j1; j += 32) {
+    float gf[VEC], uf[VEC];
+    Chunk<Tw>::widen(gp[j], gf);
+    Chunk<Tw>::widen(up[j], uf);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float4* xv = reinterpret_cast<const float4*>(xs + t * H + c0 + j * VEC);
+#pragma unroll
+      for (int q4 = 0; q4 < VEC / 4; ++q4) {
+        const float4 x4 = xv[q4];
+        float& ga = (q4 & 1) ? g1[t] : g[t];
+        float& ua = (q4 & 1) ? u1[t] : u[t];
+        ga = fmaf(gf[4 * q4 + 0], x4.x, ga);
+        ga = fmaf(gf[4 * q4 + 1], x4.y, ga);
+        ga = fmaf(gf[4 * q4 + 2], x4.z, ga);
+        ga = fmaf(gf[4 * q4 + 3], x4.w, ga);
+        ua = fmaf(uf[4 * q4 + 0], x4.x, ua);
+        ua = fmaf(uf[4 * q4 + 1], x4.y, ua);
+        ua = fmaf(uf[4 * q4 + 2], x4.z, ua);
+        ua = fmaf(uf[4 * q4 + 3], x4.w, ua);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    g[t] += g1[t];
+    u[t] += u1[t];
+  }
+}
+
+// Phase B dot of one down-row piece over chunks [0, nch) against the
+// activation window (layout [column][NT]).
+template <typename Tw, int NT>
+WR_DEVINL void dot_down(const uint4* __restrict__ wp, const float* __restrict__ av, int nch,
+                        int lane, float (&acc)[NT]) {
+  constexpr int VEC = Chunk<Tw>::kVec;
+  float acc1[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc1[t] = 0.0f;
+#pragma unroll 4
+  for (int j = lane; j < nch; j += 32) {
+    float wf[VEC];
+    Chunk<Tw>::widen(wp[j], wf);
+    const float4* a4p = reinterpret_cast<const float4*>(av + j * VEC * NT);
+#pragma unroll
+    for (int q4 = 0; q4 < VEC * NT / 4; ++q4) {
+      const float4 a4 = a4p[q4];
+      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+      for (int z = 0; z < 4; ++z) {
+        const int flat = 4 * q4 + z;  // = q * NT + t
+        float& ac = ((flat / NT) & 1) ? acc1[flat % NT] : acc[flat % NT];
+        ac = fmaf(wf[flat / NT], av4[z], ac);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] += acc1[t];
+}
+
+template <int NT>
+WR_DEVINL void warp_sum(float (&v)[NT]) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v[t] += __shfl_xor_sync(0xffffffffu, v[t], off);
+  }
+}
+
+// Position in the ring: stage slot and the parity of its current use,
+// advanced one stage at a time without divisions.
+struct Cursor {
+  int si;
+  uint32_t ph;
+  WR_DEVINL void next(int nst) {
+    if (++si == nst) {
+      si = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// Phase A row groups of one CTA, in its rotated order: groups of up to GA
+// consecutive row pairs of one slot, over the CTA's rows [pa0, pa1).
+struct UnitsA {
+  int pa0, pa1, I, GA;
+  int s, r, hi;  // current group: rows [r, min(r + GA, hi)) of slot s
+  WR_DEVINL void seg(int slot) {
+    s = slot;
+    r = max(pa0, s * I);
+    hi = min(pa1, (s + 1) * I);
+  }
+  // Places the cursor on group number `u` of the natural order.
+  WR_DEVINL void init(int pa0_, int pa1_, int I_, int GA_, int u) {
+    pa0 = pa0_; pa1 = pa1_; I = I_; GA = GA_;
+    seg(pa0 / I);
+    for (;;) {
+      const int n = (hi - r + GA - 1) / GA;
+      if (u < n || n <= 0) { r += u * GA; return; }
+      u -= n;
+      seg(s + 1);
+    }
+  }
+  WR_DEVINL int g() const { return min(GA, hi - r); }
+  WR_DEVINL void next() {
+    r += GA;
+    if (r >= hi) {
+      if (hi >= pa1) seg(pa0 / I);  // wrap to the start of the range
+      else seg(s + 1);
+    }
+  }
+};
+
+WR_DEVINL int count_units_a(int pa0, int pa1, int I, int GA) {
+  int n = 0;
+  for (int s = pa0 / I; s * I < pa1; ++s) {
+    const int lo = max(pa0, s * I), hi = min(pa1, (s + 1) * I);
+    n += (hi - lo + GA - 1) / GA;
+  }
+  return n;
+}
 
 template <typename Tw, int NT>
 __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a) {
   constexpr int VEC = Chunk<Tw>::kVec;
   constexpr int ELT = (int)sizeof(Tw);
-  constexpr int CWA = kStageBytes / (2 * kConsumerWarps * ELT);  // phase A columns per stage
-  constexpr int CWB = kStageBytes / (kConsumerWarps * ELT);      // phase B columns per stage
+  constexpr int W = kConsumerWarps;
 
   extern __shared__ __align__(1024) uint8_t smem[];
+  const Plan pl = a.pl;
+  const int nst = pl.nst;
   uint8_t* ring = smem;
-  float* vreg = reinterpret_cast<float*>(smem + kRingBytes);
-  uint8_t* misc = smem + kRingBytes + kVecBytes;
+  float* vreg = reinterpret_cast<float*>(smem + nst * pl.SB);
+  uint8_t* misc = smem + kMiscOff;
   uint64_t* full = reinterpret_cast<uint64_t*>(misc + kOffBars);
-  uint64_t* empty = full + kStages;
-  uint64_t* actbar = empty + kStages;
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* actbar = empty + kMaxStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + kOffAbort);
   int* s_nslots = reinterpret_cast<int*>(misc + kOffNSlots);
+  volatile int* slot_tag = reinterpret_cast<volatile int*>(misc + kOffSlotTag);
   int* slot_e = reinterpret_cast<int*>(misc + kOffSlotE);
   float* slot_w = reinterpret_cast<float*>(misc + kOffSlotW);
-  float* s_logits = reinterpret_cast<float*>(misc + kOffLogits);
   int* tok_ids = reinterpret_cast<int*>(misc + kOffTokIds);
   float* tok_w = reinterpret_cast<float*>(misc + kOffTokW);
+  float* rowacc = reinterpret_cast<float*>(misc + kOffRowAcc);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -111,9 +332,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   const int G = gridDim.x, b = blockIdx.x;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < nst; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], W);
+      slot_tag[s] = -1;
     }
     mbar_init(actbar, 1);
     *abort_flag = 0;
@@ -123,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   // ---- x -> shared memory as fp32 [NT][H] (tokens >= T are zero) ----------
   {
     const Tw* xg = static_cast<const Tw*>(a.x);
-    const int nvec = H / VEC;  // host guarantees H % VEC == 0 on this path
+    const int nvec = H / VEC;  // the host guarantees H % VEC == 0 on this path
     for (int idx = tid; idx < NT * nvec; idx += kThreads) {
       const int t = idx / nvec;
       const int v = idx - t * nvec;
@@ -134,32 +356,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 #pragma unroll
         for (int q = 0; q < VEC; ++q) f[q] = 0.0f;
       }
-      float4* dst = reinterpret_cast<float4*>(vreg + (int64_t)t * H + (int64_t)v * VEC);
+      float4* dst = reinterpret_cast<float4*>(vreg + t * H + v * VEC);
 #pragma unroll
-      for (int q = 0; q < VEC / 4; ++q) dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+      for (int q = 0; q < VEC / 4; ++q)
+        dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
     }
   }
-  __syncthreads();
 
-  // ---- router: every warp takes (token, expert) pairs ----------------------
-  for (int j = warp; j < T * E; j += kThreads / 32) {
-    const int t = j / E;
-    const int e = j - t * E;
-    float l = router_logit_warp<Tw>(static_cast<const Tw*>(a.gate_w) + (int64_t)e * H,
-                                    vreg + (int64_t)t * H, H, lane, true);
-    if (lane == 0) {
-      if (a.router_bias) l = __fadd_rn(l, a.router_bias[e]);
-      s_logits[t * kMaxExperts + e] = l;
-    }
-  }
+  // ---- routing: logits come from k_router_logits (the grid we depend on) --
+  griddep_wait();
+  if (warp < T)
+    select_topk_warp(a.logits + warp * E, E, K, lane, tok_ids + warp * kMaxExperts,
+                     tok_w + warp * kMaxExperts);
   __syncthreads();
-
-  // ---- selection + slots (one thread; E <= 64, K <= E) ---------------------
   if (tid == 0) {
     int ns = 0;
     for (int t = 0; t < T; ++t) {
-      softmax_topk(s_logits + t * kMaxExperts, E, K, tok_ids + t * kMaxExperts,
-                   tok_w + t * kMaxExperts);
       for (int k = 0; k < K; ++k) {
         const int e = tok_ids[t * kMaxExperts + k];
         if (e < a.ep_first || e >= a.ep_first + a.ep_num) continue;
@@ -173,29 +385,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         }
         slot_w[s * NT + t] = tok_w[t * kMaxExperts + k];
       }
-      if (b == 0) {
-        for (int k = 0; k < K; ++k) {
-          if (a.ids_out) a.ids_out[t * K + k] = tok_ids[t * kMaxExperts + k];
-          if (a.w_out) a.w_out[t * K + k] = tok_w[t * kMaxExperts + k];
-        }
-      }
     }
     *s_nslots = ns;
+  }
+  if (b == 0) {
+    for (int i = tid; i < T * K; i += kThreads) {
+      const int t = i / K, k = i - t * K;
+      if (a.ids_out) a.ids_out[i] = tok_ids[t * kMaxExperts + k];
+      if (a.w_out) a.w_out[i] = tok_w[t * kMaxExperts + k];
+    }
   }
   __syncthreads();
 
   const int S = *s_nslots;
-  const int64_t P = (int64_t)S * I;  // phase A rows == phase B columns
-  const int pa0 = split_lo(P, b, G), pa1 = split_lo(P, b + 1, G);
-  const int hb0 = split_lo(H, b, G), hb1 = split_lo(H, b + 1, G);
-  const int na = pa1 - pa0, nb = hb1 - hb0;
-  const int nga = (na + kConsumerWarps - 1) / kConsumerWarps;
-  const int ngb = (nb + kConsumerWarps - 1) / kConsumerWarps;
-  // Activation windows over the P columns of phase B.
-  const int64_t wmax = (int64_t)(kVecBytes / (NT * 4)) / VEC * VEC;
-  const int nwin = (int)((P + wmax - 1) / wmax);
-  int64_t wsz = nwin ? (P + nwin - 1) / nwin : 0;
-  wsz = (wsz + VEC - 1) / VEC * VEC;
+  const int P = S * I;  // phase A rows (S <= 64, I < 2^25)
+  const int pa0 = (int)split_lo(P, b, G), pa1 = (int)split_lo(P, b + 1, G);
+  const int hb0 = (int)split_lo(H, b, G), hb1 = (int)split_lo(H, b + 1, G);
+  const int nb = hb1 - hb0;
+  const int na_u = pa1 > pa0 ? count_units_a(pa0, pa1, I, pl.GA) : 0;
+  const int rot_a = na_u ? (int)(((int64_t)b * 37) % na_u) : 0;
+  const int nb_u = (nb + pl.GB - 1) / pl.GB;
+  const int hb_start = hb0 + (nb_u ? (int)(((int64_t)b * 11) % nb_u) : 0) * pl.GB;
+  const int wc_last = I - (pl.nwin - 1) * pl.WB;  // width of a slot's last window
 
   if (S == 0) {
     // No local expert selected (expert-parallel rank): this rank adds zero.
@@ -203,147 +414,188 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       const int t = idx / nb;
       a.out[(int64_t)t * H + hb0 + (idx - t * nb)] = 0.0f;
     }
-  } else if (warp == kConsumerWarps) {
+  } else if (warp == W) {
     // =========================== producer ===================================
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      uint32_t it = 0;
       bool ok = true;
-      for (int gi = 0; gi < nga && ok; ++gi) {
-        const int r0 = pa0 + split_lo(na, gi, nga), r1 = pa0 + split_lo(na, gi + 1, nga);
-        for (int c0 = 0; c0 < H; c0 += CWA) {
-          const int cw = min(CWA, H - c0);
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-          uint8_t* st = ring + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * (r1 - r0) * cw * ELT));
-          for (int r = r0; r < r1; ++r) {
-            const int sl = r / I;
-            const int i = r - sl * I;
-            const uint8_t* src = a.wbuf + (int64_t)slot_e[sl] * a.lay.stride +
-                                 ((int64_t)i * H + c0) * ELT;
-            bulk_g2s(st + (r - r0) * CWA * ELT, src + a.lay.off_gate, cw * ELT, &full[s], pol);
-            bulk_g2s(st + (kConsumerWarps + r - r0) * CWA * ELT, src + a.lay.off_up, cw * ELT,
-                     &full[s], pol);
-          }
-          ++it;
+      int issued = 0;
+      Cursor c{0, 0u};
+      // Reserves the next stage: waits for the stage it replaces to be
+      // released, then tags the slot with the new stage number.  Returns
+      // false on a timeout.
+      auto reserve = [&]() -> bool {
+        if (issued >= nst && !mbar_wait(&empty[c.si], c.ph ^ 1u, abort_flag)) return false;
+        slot_tag[c.si] = issued;
+        return true;
+      };
+      // Owners of rows [base, base + g) (mod W) release the stage; arrive
+      // for the other warps now.
+      auto commit = [&](int g) {
+        const int owners = g < W ? g : W;
+        if (owners < W) mbar_arrive_cnt(&empty[c.si], (uint32_t)(W - owners));
+        c.next(nst);
+        ++issued;
+      };
+      // phase A
+      UnitsA u;
+      u.init(pa0, pa1, I, pl.GA, rot_a);
+      for (int uu = 0; uu < na_u && ok; ++uu, u.next()) {
+        const int g = u.g();
+        const uint8_t* eb = a.wbuf + (int64_t)slot_e[u.s] * a.lay.stride +
+                            (int64_t)(u.r - u.s * I) * H * ELT;
+        for (int c0 = 0; c0 < H; c0 += pl.CWA) {
+          if (!(ok = reserve())) break;
+          const int cw = min(pl.CWA, H - c0);
+          uint8_t* st = ring + c.si * pl.SB;
+          const uint32_t piece = (uint32_t)g * cw * ELT;  // g == 1 when cw < H
+          mbar_arrive_expect_tx(&full[c.si], 2 * piece);
+          const uint8_t* src = eb + (int64_t)c0 * ELT;
+          bulk_g2s(st, src + a.lay.off_gate, piece, &full[c.si], pol);
+          bulk_g2s(st + pl.GA * pl.CWA * ELT, src + a.lay.off_up, piece, &full[c.si], pol);
+          commit(g);
         }
       }
-      for (int w = 0; w < nwin && ok; ++w) {
-        const int64_t ws0 = (int64_t)w * wsz;
-        const int64_t ws1 = min(P, ws0 + wsz);
-        for (int gi = 0; gi < ngb && ok; ++gi) {
-          const int r0 = hb0 + split_lo(nb, gi, ngb), r1 = hb0 + split_lo(nb, gi + 1, ngb);
-          for (int64_t c0 = ws0; c0 < ws1; c0 += CWB) {
-            const int cw = (int)min((int64_t)CWB, ws1 - c0);
-            const int s = it % kStages;
-            const uint32_t ph = (it / kStages) & 1u;
-            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-            uint8_t* st = ring + s * kStageBytes;
-            mbar_arrive_expect_tx(&full[s], (uint32_t)((r1 - r0) * cw * ELT));
-            for (int r = r0; r < r1; ++r) {
-              uint8_t* dst = st + (r - r0) * CWB * ELT;
-              int64_t c = c0;
-              while (c < c0 + cw) {
-                const int sl = (int)(c / I);
-                const int64_t i0 = c - (int64_t)sl * I;
-                const int len = (int)(min(c0 + cw, (int64_t)(sl + 1) * I) - c);
-                const uint8_t* src = a.wbuf + (int64_t)slot_e[sl] * a.lay.stride +
-                                     a.lay.off_down + ((int64_t)r * I + i0) * ELT;
-                bulk_g2s(dst + (c - c0) * ELT, src, len * ELT, &full[s], pol);
-                c += len;
-              }
+      // phase B
+      for (int s = 0; s < S && ok; ++s) {
+        const uint8_t* eb = a.wbuf + (int64_t)slot_e[s] * a.lay.stride + a.lay.off_down;
+        for (int win = 0, c0 = 0; win < pl.nwin && ok; ++win, c0 += pl.WB) {
+          const int wc = win + 1 < pl.nwin ? pl.WB : wc_last;
+          int hb = hb_start;
+          for (int uu = 0; uu < nb_u; ++uu) {
+            if (!(ok = reserve())) break;
+            const int g = min(pl.GB, hb1 - hb);
+            uint8_t* st = ring + c.si * pl.SB;
+            const uint8_t* src = eb + ((int64_t)hb * I + c0) * ELT;
+            mbar_arrive_expect_tx(&full[c.si], (uint32_t)g * wc * ELT);
+            if (wc == I) {
+              bulk_g2s(st, src, (uint32_t)g * I * ELT, &full[c.si], pol);
+            } else {
+              for (int r = 0; r < g; ++r)
+                bulk_g2s(st + r * pl.WB * ELT, src + (int64_t)r * I * ELT, wc * ELT, &full[c.si],
+                         pol);
             }
-            ++it;
+            commit(g);
+            hb += pl.GB;
+            if (hb >= hb1) hb = hb0;
           }
         }
       }
       if (!ok) {
         // Let every copy already issued land before the CTA can exit.
         *abort_flag = 1;
-        const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0u;
-        for (uint32_t j = first; j < it; ++j)
-          if (!mbar_wait(&full[j % kStages], (j / kStages) & 1u, nullptr))
+        const int first = issued > nst ? issued - nst : 0;
+        for (int j = first; j < issued; ++j)
+          if (!mbar_wait(&full[j % nst], (uint32_t)(j / nst) & 1u, nullptr))
             atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
         atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_EMPTY);
       }
     }
   } else {
-    // =========================== consumers ==================================
-    // Abort-safe structure: loop trip counts depend only on the problem, so
-    // every consumer warp passes every named barrier exactly once even after
-    // a failed wait; `ok` is kept warp-uniform with __all_sync.
-    const int cw_id = warp;  // 0..7
-    uint32_t it = 0;
+    // =========================== consumer warps =============================
+    // Only the owners of a stage's rows wait for it, read it and release it.
+    // Loop trip counts depend only on the problem, so all warps pass every
+    // named barrier exactly once even after a failed wait; `ok` is kept
+    // warp-uniform with __all_sync.
+    Cursor c{0, 0u};
+    int stage = 0;  // number of the stage under the cursor
     bool ok = true;
-    // ---- phase A: gate/up rows -> activations ----
-    for (int gi = 0; gi < nga; ++gi) {
-      const int r0 = pa0 + split_lo(na, gi, nga), r1 = pa0 + split_lo(na, gi + 1, nga);
-      const bool active = cw_id < r1 - r0;
-      float g[NT], u[NT];
+    // Owner's wait for stage `stage` in slot c.si: its tag, then its data.
+    auto wait_owned = [&]() -> bool {
+      bool got = true;
+      if (slot_tag[c.si] != stage) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t spin = 1; slot_tag[c.si] != stage; ++spin) {
+          if ((spin & 63u) == 0 && (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
+            got = false;
+            break;
+          }
+        }
+      }
+      if (got) got = mbar_wait(&full[c.si], c.ph, abort_flag);
+      return __all_sync(0xffffffffu, got);
+    };
+
+    // ---- phase A: gate/up rows -> activations; row pair p owned by warp p%8 ----
+    {
+      const int nch_full = pl.CWA / VEC;
+      float ga[NT], ua[NT];  // running sums of a row pair split over stages
 #pragma unroll
-      for (int t = 0; t < NT; ++t) g[t] = u[t] = 0.0f;
-      for (int c0 = 0; c0 < H; c0 += CWA) {
-        const int cw = min(CWA, H - c0);
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1u;
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag));
-        if (ok && active) {
-          const uint8_t* st = ring + s * kStageBytes;
-          const uint4* gp = reinterpret_cast<const uint4*>(st + cw_id * CWA * ELT);
-          const uint4* up = reinterpret_cast<const uint4*>(st + (kConsumerWarps + cw_id) * CWA * ELT);
-          const int nch = cw / VEC;
-          for (int j = lane; j < nch; j += 32) {
-            float gf[VEC], uf[VEC];
-            Chunk<Tw>::widen(gp[j], gf);
-            Chunk<Tw>::widen(up[j], uf);
+      for (int t = 0; t < NT; ++t) ga[t] = ua[t] = 0.0f;
+      UnitsA u;
+      u.init(pa0, pa1, I, pl.GA, rot_a);
+      for (int uu = 0; uu < na_u; ++uu, u.next()) {
+        const int g = u.g();
+        const int first = (warp - (u.r & (W - 1)) + W) & (W - 1);  // my first row of the group
+        const bool mine = first < g;
+        for (int c0 = 0; c0 < H; c0 += pl.CWA) {
+          const int cw = min(pl.CWA, H - c0);
+          if (ok && mine) ok = wait_owned();
+          if (ok && mine) {
+            const uint8_t* st = ring + c.si * pl.SB;
+            if (cw == H) {
+              // whole row pairs: rows first, first+8, ... of this stage
+              float gg[kRowsPerWarp][NT], uv[kRowsPerWarp][NT];
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const float4* xv = reinterpret_cast<const float4*>(vreg + (int64_t)t * H + c0 + j * VEC);
+              for (int k = 0; k < kRowsPerWarp; ++k) {
 #pragma unroll
-              for (int q4 = 0; q4 < VEC / 4; ++q4) {
-                const float4 x4 = xv[q4];
-                g[t] = fmaf(gf[4 * q4 + 0], x4.x, g[t]);
-                g[t] = fmaf(gf[4 * q4 + 1], x4.y, g[t]);
-                g[t] = fmaf(gf[4 * q4 + 2], x4.z, g[t]);
-                g[t] = fmaf(gf[4 * q4 + 3], x4.w, g[t]);
-                u[t] = fmaf(uf[4 * q4 + 0], x4.x, u[t]);
-                u[t] = fmaf(uf[4 * q4 + 1], x4.y, u[t]);
-                u[t] = fmaf(uf[4 * q4 + 2], x4.z, u[t]);
-                u[t] = fmaf(uf[4 * q4 + 3], x4.w, u[t]);
+                for (int t = 0; t < NT; ++t) gg[k][t] = uv[k][t] = 0.0f;
+                const int rr = first + k * W;
+                if (rr < g)
+                  dot_pair<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.CWA * ELT),
+                                   reinterpret_cast<const uint4*>(st + (pl.GA + rr) * pl.CWA * ELT),
+                                   vreg, H, 0, 0, nch_full, lane, gg[k], uv[k]);
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[c.si]);
+#pragma unroll
+              for (int k = 0; k < kRowsPerWarp; ++k) {
+                const int rr = first + k * W;
+                if (rr < g) {
+                  warp_sum<NT>(gg[k]);
+                  warp_sum<NT>(uv[k]);
+#pragma unroll
+                  for (int t = 0; t < NT; ++t) {
+                    if (lane == t) {
+                      const float wt = slot_w[u.s * NT + t];
+                      a.act[((int64_t)u.r + rr) * NT + t] =
+                          (wt != 0.0f) ? wt * (silu(gg[k][t]) * uv[k][t]) : 0.0f;
+                    }
+                  }
+                }
+              }
+            } else {
+              // one row pair split over several stages (g == 1, first == 0)
+              dot_pair<Tw, NT>(reinterpret_cast<const uint4*>(st),
+                               reinterpret_cast<const uint4*>(st + pl.GA * pl.CWA * ELT), vreg, H,
+                               c0, 0, cw / VEC, lane, ga, ua);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[c.si]);
+              if (c0 + cw >= H) {
+                warp_sum<NT>(ga);
+                warp_sum<NT>(ua);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                  if (lane == t) {
+                    const float wt = slot_w[u.s * NT + t];
+                    a.act[(int64_t)u.r * NT + t] = (wt != 0.0f) ? wt * (silu(ga[t]) * ua[t]) : 0.0f;
+                  }
+                }
+#pragma unroll
+                for (int t = 0; t < NT; ++t) ga[t] = ua[t] = 0.0f;
               }
             }
           }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        ++it;
-      }
-      if (ok && active) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) {
-            g[t] += __shfl_xor_sync(0xffffffffu, g[t], off);
-            u[t] += __shfl_xor_sync(0xffffffffu, u[t], off);
-          }
-        }
-        if (lane == 0) {
-          const int r = r0 + cw_id;
-          const int sl = r / I;
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const float wt = slot_w[sl * NT + t];
-            a.act[(int64_t)r * NT + t] = (wt != 0.0f) ? wt * (silu(g[t]) * u[t]) : 0.0f;
-          }
+          c.next(nst);
+          ++stage;
         }
       }
     }
     if (!ok && lane == 0) *abort_flag = 1;
+    for (int i = tid; i < nb * NT; i += kConsumerThreads) rowacc[i] = 0.0f;
 
     // ---- grid-wide barrier: every CTA's activations are written ----
-    named_bar_sync(1, kConsumerThreads);
+    named_bar_sync(kBarConsumers, kConsumerThreads);
     if (tid == 0) {
       __threadfence();
       fence_proxy_async_global();
@@ -362,83 +614,84 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       fence_proxy_async_global();
     }
 
-    // ---- phase B: down rows over activation windows ----
-    int act_issued = 0;
-    for (int w = 0; w < nwin; ++w) {
-      const int64_t ws0 = (int64_t)w * wsz;
-      const int64_t ws1 = min(P, ws0 + wsz);
-      named_bar_sync(1, kConsumerThreads);  // window w-1 fully read (or the grid barrier done)
-      if (*abort_flag) ok = false;
-      if (tid == 0 && ok) {
-        fence_proxy_async_smem();
-        const uint32_t bytes = (uint32_t)((ws1 - ws0) * NT * 4);
-        const uint64_t pol = l2_policy_evict_last();
-        mbar_arrive_expect_tx(actbar, bytes);
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(a.act + ws0 * NT);
-        for (uint32_t off = 0; off < bytes; off += 32768u)
-          bulk_g2s(reinterpret_cast<uint8_t*>(vreg) + off, src + off, min(32768u, bytes - off),
-                   actbar, pol);
-        act_issued = w + 1;
-      }
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(actbar, (uint32_t)(w & 1), abort_flag));
-      for (int gi = 0; gi < ngb; ++gi) {
-        const int r0 = hb0 + split_lo(nb, gi, ngb), r1 = hb0 + split_lo(nb, gi + 1, ngb);
-        const bool active = cw_id < r1 - r0;
-        float acc[NT];
+    // ---- phase B: down rows, slot by slot; local row h owned by warp h%8 ----
+    {
+      uint32_t aw = 0;
+      int act_issued = 0;
+      for (int s = 0; s < S; ++s) {
+        for (int win = 0, c0 = 0; win < pl.nwin; ++win, c0 += pl.WB) {
+          const int wc = win + 1 < pl.nwin ? pl.WB : wc_last;
+          const int nch = wc / VEC;
+          named_bar_sync(kBarConsumers, kConsumerThreads);  // previous window fully read
+          if (*abort_flag) ok = false;
+          if (tid == 0 && ok) {
+            fence_proxy_async_smem();
+            const uint32_t bytes = (uint32_t)wc * NT * 4;
+            const uint64_t pol = l2_policy_evict_last();
+            mbar_arrive_expect_tx(actbar, bytes);
+            const uint8_t* src =
+                reinterpret_cast<const uint8_t*>(a.act + ((int64_t)s * I + c0) * NT);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+              bulk_g2s(reinterpret_cast<uint8_t*>(vreg) + off, src + off, min(32768u, bytes - off),
+                       actbar, pol);
+            act_issued = (int)aw + 1;
+          }
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(actbar, aw & 1u, abort_flag));
+          ++aw;
+          int hb = hb_start;
+          for (int uu = 0; uu < nb_u; ++uu) {
+            const int g = min(pl.GB, hb1 - hb);
+            const int first = (warp - ((hb - hb0) & (W - 1)) + W) & (W - 1);
+            if (ok && first < g) ok = wait_owned();
+            if (ok && first < g) {
+              const uint8_t* st = ring + c.si * pl.SB;
+              float v[kRowsPerWarp][NT];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        for (int64_t c0 = ws0; c0 < ws1; c0 += CWB) {
-          const int cw = (int)min((int64_t)CWB, ws1 - c0);
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
-          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag));
-          if (ok && active) {
-            const uint4* wp = reinterpret_cast<const uint4*>(ring + s * kStageBytes + cw_id * CWB * ELT);
-            const float* abase = vreg + (c0 - ws0) * NT;
-            const int nch = cw / VEC;
-            for (int j = lane; j < nch; j += 32) {
-              float wf[VEC];
-              Chunk<Tw>::widen(wp[j], wf);
-              const float4* av = reinterpret_cast<const float4*>(abase + j * VEC * NT);
+              for (int k = 0; k < kRowsPerWarp; ++k) {
 #pragma unroll
-              for (int q4 = 0; q4 < VEC * NT / 4; ++q4) {
-                const float4 a4 = av[q4];
-                const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
+                for (int t = 0; t < NT; ++t) v[k][t] = 0.0f;
+                const int rr = first + k * W;
+                if (rr < g)
+                  dot_down<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.WB * ELT), vreg, nch,
+                                   lane, v[k]);
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[c.si]);
 #pragma unroll
-                for (int z = 0; z < 4; ++z) {
-                  const int flat = 4 * q4 + z;  // = q * NT + t
-                  acc[flat % NT] = fmaf(wf[flat / NT], av4[z], acc[flat % NT]);
+              for (int k = 0; k < kRowsPerWarp; ++k) {
+                const int rr = first + k * W;
+                if (rr < g) {
+                  warp_sum<NT>(v[k]);
+                  if (lane == 0) {
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) rowacc[(hb - hb0 + rr) * NT + t] += v[k][t];
+                  }
                 }
               }
             }
+            c.next(nst);
+            ++stage;
+            hb += pl.GB;
+            if (hb >= hb1) hb = hb0;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[s]);
-          ++it;
-        }
-        if (ok && active) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], off);
-          }
-          if (lane == 0) {
-            const int h = r0 + cw_id;
-            for (int t = 0; t < T; ++t) {
-              float* o = a.out + (int64_t)t * H + h;
-              *o = (w == 0) ? acc[t] : *o + acc[t];
-            }
-          }
+          if (!ok && lane == 0) *abort_flag = 1;
         }
       }
-      if (!ok && lane == 0) *abort_flag = 1;
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // all row accumulators final
+      if (ok && !*abort_flag) {
+        for (int idx = tid; idx < T * nb; idx += kConsumerThreads) {
+          const int t = idx / nb;
+          const int h = idx - t * nb;
+          a.out[(int64_t)t * H + hb0 + h] = rowacc[h * NT + t];
+        }
+      }
+      if (tid == 0 && act_issued > 0 && !ok) {
+        // The last activation copy must land before the CTA exits.
+        if (!mbar_wait(actbar, (uint32_t)((act_issued - 1) & 1), nullptr))
+          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
+      }
+      if (lane == 0 && !ok) atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_FULL);
     }
-    if (tid == 0 && act_issued > 0 && !ok) {
-      // The last activation copy must land before the CTA exits.
-      if (!mbar_wait(actbar, (uint32_t)((act_issued - 1) & 1), nullptr))
-        atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
-    }
-    if (lane == 0 && !ok) atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_FULL);
   }
 
   __syncthreads();
@@ -455,34 +708,114 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   }
 }
 
+// Launch mode of the fused kernel, probed once per device: programmatic
+// dependent launch together with the cooperative attribute when the driver
+// takes both, else each alone.
+enum LaunchMode { kModeUnknown = 0, kModeCoopPdl, kModePdl, kModeCoop };
+
 template <typename Tw, int NT>
-wr_status_t launch_one(const FusedArgs& args, int grid, cudaStream_t stream) {
+wr_status_t launch_pair(const FusedArgs& args, const void* x, const void* gate_w,
+                        const float* bias, float* logits, int grid, cudaStream_t stream) {
   auto kern = k_fused_stream<Tw, NT>;
+  auto rkern = k_router_logits<Tw>;
   static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  static int mode[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  static cudaError_t attr_err[64];
   std::call_once(once[dev & 63], [&] {
     attr_err[dev & 63] =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (attr_err[dev & 63] == cudaSuccess)
+      attr_err[dev & 63] = cudaFuncSetAttribute(
+          rkern, cudaFuncAttributeMaxDynamicSharedMemorySize, kVecMaxBytes);
   });
-  if (attr_err[dev & 63] != cudaSuccess) return cuda_fail(attr_err[dev & 63], "cudaFuncSetAttribute(fused)");
+  if (attr_err[dev & 63] != cudaSuccess)
+    return cuda_fail(attr_err[dev & 63], "cudaFuncSetAttribute(fused)");
+
+  // 1. router logits
+  const int H = args.H, E = args.E, T = args.T;
+  dim3 rgrid((E + 7) / 8, T);
+  rkern<<<rgrid, kConsumerThreads, (size_t)H * sizeof(float), stream>>>(
+      static_cast<const Tw*>(x), static_cast<const Tw*>(gate_w), bias, E, H, logits);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "k_router_logits launch");
+
+  // 2. the streaming kernel, dependent on (1)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(fused)");
-  return WR_OK;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  int& m = mode[dev & 63];
+  const int tries[3] = {kModeCoopPdl, kModePdl, kModeCoop};
+  for (int i = 0; i < 3; ++i) {
+    const int mm = m != kModeUnknown ? m : tries[i];
+    if (mm == kModeCoopPdl) { cfg.attrs = attr; cfg.numAttrs = 2; }
+    if (mm == kModePdl) { cfg.attrs = attr + 1; cfg.numAttrs = 1; }
+    if (mm == kModeCoop) { cfg.attrs = attr; cfg.numAttrs = 1; }
+    e = cudaLaunchKernelEx(&cfg, kern, args);
+    if (e == cudaSuccess) {
+      m = mm;
+      return WR_OK;
+    }
+    if (m != kModeUnknown) break;
+    cudaGetLastError();  // clear, try the next mode
+  }
+  return cuda_fail(e, "cudaLaunchKernelEx(fused)");
 }
 
 int nt_bucket(int T) { return T <= 1 ? 1 : (T <= 2 ? 2 : 4); }
+
+int clamp_rows(int64_t g) {
+  if (g < 1) g = 1;
+  return (int)(g > kMaxRowsPerStage ? kMaxRowsPerStage : g);
+}
+
+Plan make_plan(const Problem& p, int nt) {
+  const int elt = p.elt, vec = 16 / elt;
+  Plan pl;
+  // phase A: whole row pairs when one fits in a stage, else 16 KB pieces
+  const int64_t pair = 2LL * p.H * elt;
+  int stage_a;
+  if (pair <= kMaxStageBytes) {
+    pl.GA = clamp_rows(kTargetStage / pair);
+    pl.CWA = p.H;
+    stage_a = (int)(pl.GA * pair);
+  } else {
+    pl.GA = 1;
+    pl.CWA = (kTargetStage / 2 / elt) / vec * vec;
+    stage_a = 2 * pl.CWA * elt;
+  }
+  // phase B: windows of at most kTargetStage bytes of weight columns
+  int64_t wmax = (int64_t)kVecMaxBytes / (nt * 4);
+  if (wmax > kTargetStage / elt) wmax = kTargetStage / elt;
+  wmax = wmax / vec * vec;
+  if (p.I <= wmax) {
+    pl.nwin = 1;
+    pl.WB = p.I;
+  } else {
+    pl.nwin = (int)((p.I + wmax - 1) / wmax);
+    int64_t w = (p.I + pl.nwin - 1) / pl.nwin;
+    pl.WB = (int)((w + vec - 1) / vec * vec);
+  }
+  const int64_t row_b = (int64_t)pl.WB * elt;
+  int sb = stage_a > (int)row_b ? stage_a : (int)row_b;
+  sb = (sb + 127) / 128 * 128;
+  pl.GB = clamp_rows(sb / row_b);
+  pl.SB = sb;
+  int64_t need = (int64_t)nt * p.H * 4;
+  if ((int64_t)pl.WB * nt * 4 > need) need = (int64_t)pl.WB * nt * 4;
+  need = (need + 63) / 64 * 64;
+  int nst = (int)((kMiscOff - need) / sb);
+  pl.nst = nst > kMaxStages ? kMaxStages : nst;
+  return pl;
+}
 
 }  // namespace
 
@@ -492,7 +825,11 @@ bool fused_supported(const Problem& p) {
   if (p.E > kMaxExperts || p.K > p.E) return false;
   if (p.T < 1 || p.T > kMaxNT) return false;
   const int nt = nt_bucket(p.T);
-  if ((int64_t)nt * p.H * 4 > kVecBytes) return false;  // x must fit in shared memory
+  if ((int64_t)nt * p.H * 4 > kVecMaxBytes) return false;  // x must fit in shared memory
+  if ((int64_t)p.K * nt * p.I >= (1LL << 30)) return false; // 32-bit row indices
+  const int grid = device_sm_count();
+  const int64_t rows = ((int64_t)p.H + grid - 1) / grid;
+  if (rows * nt > kRowAccFloats) return false;             // phase-B row accumulators
   return true;
 }
 
@@ -500,21 +837,21 @@ size_t fused_workspace_bytes(const Problem& p) {
   const int nt = nt_bucket(p.T < 1 ? 1 : p.T);
   const int64_t slots = p.ep_num < p.K * nt ? p.ep_num : (int64_t)p.K * nt;
   const size_t act = (size_t)slots * p.I * nt * sizeof(float);
-  return kSyncBytes + ((act + 255) & ~size_t(255));
+  return kActOffset + ((act + 255) & ~size_t(255));
 }
 
 wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, const void* wbuf,
                          float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream) {
   FusedArgs args;
   args.x = x;
-  args.gate_w = gate_w;
-  args.router_bias = p.router_bias;
   args.wbuf = static_cast<const uint8_t*>(wbuf);
   args.out = out;
   args.ids_out = ids;
   args.w_out = w;
   args.sync = static_cast<uint32_t*>(ws);
-  args.act = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSyncBytes);
+  float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSyncBytes);
+  args.logits = logits;
+  args.act = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kActOffset);
   args.E = p.E;
   args.H = p.H;
   args.I = p.I;
@@ -523,16 +860,18 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
   args.ep_first = p.ep_first;
   args.ep_num = p.ep_num;
   args.lay = make_layout(p.H, p.I, p.elt);
-  const int grid = device_sm_count();
   const int nt = nt_bucket(p.T);
+  args.pl = make_plan(p, nt);
+  const int grid = device_sm_count();
+  const float* bias = p.router_bias;
   if (p.dtype == WR_DTYPE_BF16) {
-    if (nt == 1) return launch_one<uint16_t, 1>(args, grid, stream);
-    if (nt == 2) return launch_one<uint16_t, 2>(args, grid, stream);
-    return launch_one<uint16_t, 4>(args, grid, stream);
+    if (nt == 1) return launch_pair<uint16_t, 1>(args, x, gate_w, bias, logits, grid, stream);
+    if (nt == 2) return launch_pair<uint16_t, 2>(args, x, gate_w, bias, logits, grid, stream);
+    return launch_pair<uint16_t, 4>(args, x, gate_w, bias, logits, grid, stream);
   }
-  if (nt == 1) return launch_one<float, 1>(args, grid, stream);
-  if (nt == 2) return launch_one<float, 2>(args, grid, stream);
-  return launch_one<float, 4>(args, grid, stream);
+  if (nt == 1) return launch_pair<float, 1>(args, x, gate_w, bias, logits, grid, stream);
+  if (nt == 2) return launch_pair<float, 2>(args, x, gate_w, bias, logits, grid, stream);
+  return launch_pair<float, 4>(args, x, gate_w, bias, logits, grid, stream);
 }
 
 }  // namespace wr

@@ -20,7 +20,9 @@
 namespace wr {
 namespace {
 
-constexpr int kRouterThreads = 256;
+constexpr int kRouterThreads = 32 * kRouterSegments;
+// k_router's static shared memory (segment partials, logits, ids, weights).
+constexpr int kRouterStaticSmem = 4 * (kRouterSegments * kMaxExperts + 3 * kMaxExperts);
 
 // One CTA per token: x -> shared memory (fp32), logits by warps, softmax +
 // top-K by thread 0.
@@ -33,6 +35,7 @@ __global__ void __launch_bounds__(kRouterThreads) k_router(const Tw* __restrict_
                                                            int32_t* __restrict__ ids_out,
                                                            float* __restrict__ w_out) {
   extern __shared__ __align__(16) float xs[];
+  __shared__ float parts[kRouterSegments * kMaxExperts];
   __shared__ float lg[kMaxExperts];
   __shared__ int ids[kMaxExperts];
   __shared__ float ws[kMaxExperts];
@@ -41,14 +44,16 @@ __global__ void __launch_bounds__(kRouterThreads) k_router(const Tw* __restrict_
   for (int h = threadIdx.x; h < H; h += blockDim.x) xs[h] = load_scalar<Tw>(xt, h);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = warp; e < E; e += blockDim.x / 32) {
-    float l = router_logit_warp<Tw>(gate_w + (int64_t)e * H, xs, H, lane, vec_ok);
-    if (lane == 0) lg[e] = bias ? __fadd_rn(l, bias[e]) : l;
-  }
+  // blockDim.x == 32 * kRouterSegments: warp j computes segment j of every row.
+  router_segment_warp<Tw>(gate_w, xs, E, H, warp, lane, vec_ok, parts + warp * kMaxExperts);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    softmax_topk(lg, E, K, ids, ws);
-    for (int k = 0; k < K; ++k) {
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    lg[e] = router_combine(parts, kMaxExperts, e, bias);
+  __syncthreads();
+  if (warp == 0) {
+    select_topk_warp(lg, E, K, lane, ids, ws);
+    __syncwarp();
+    for (int k = lane; k < K; k += 32) {
       ids_out[(int64_t)t * K + k] = ids[k];
       w_out[(int64_t)t * K + k] = ws[k];
     }
@@ -114,10 +119,10 @@ wr_status_t router_impl(const Problem& p, const void* x, const void* gate_w, flo
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
     err[dev & 63] = cudaFuncSetAttribute(k_router<Tw>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         232448 - 4 * 3 * kMaxExperts);
+                                         232448 - kRouterStaticSmem);
   });
   if (err[dev & 63] != cudaSuccess) return cuda_fail(err[dev & 63], "cudaFuncSetAttribute(router)");
-  if (smem > (size_t)(232448 - 4 * 3 * kMaxExperts))
+  if (smem > (size_t)(232448 - kRouterStaticSmem))
     return fail(WR_ERR_UNSUPPORTED, "hidden_dim %d too large for the router kernel", p.H);
   const int vec = 16 / p.elt;
   const bool vec_ok = (p.H % vec == 0) && ((reinterpret_cast<uintptr_t>(gate_w) & 15) == 0);

@@ -4,13 +4,17 @@
 // src/gate.cu:6-101): fp32 logits = gate_w[e,:] . x, softmax over all E,
 // iterative argmax with strict '>' (ties -> lowest index), weights are the
 // probabilities, not renormalised.  Differences, on purpose:
-//   * one fixed reduction order for each logit — lane l of a warp runs an
-//     explicit-fma sweep over the 16-byte vectors v = l, l+32, l+64, ...
-//     (elements of a vector in order), then a 16/8/4/2/1 xor tree — so the
-//     logits are bit-identical across devices and to the CPU oracle;
+//   * one fixed reduction order for each logit, so logits are bit-identical
+//     across devices and to the CPU oracle.  The row's 16-byte vectors
+//     (nvec = ceil(H / VEC)) are cut into 8 segments [nvec*j/8,
+//     nvec*(j+1)/8); in segment j, lane l runs an explicit-fma sweep over the
+//     vectors lo+l, lo+l+32, ... (elements of a vector in order), a 16/8/4/2/1
+//     xor tree gives the segment sum s_j, and logit = (((s_0 + s_1) + s_2) +
+//     ... + s_7).  One warp per segment lets every warp keep many router rows
+//     in flight at once;
 //   * the argmax runs on the logits (softmax is monotonic), so selection
 //     never depends on the last bit of exp();
-//   * an optional fp32 router bias is added after the tree.
+//   * an optional fp32 router bias is added after the sum.
 #pragma once
 
 #include "wr_common.cuh"
@@ -18,60 +22,125 @@
 namespace wr {
 
 constexpr int kMaxExperts = 64;
+constexpr int kRouterSegments = 8;
+constexpr int kRouterRowBatch = 8;  // router rows a warp keeps in flight
 
-// One logit, computed by a full warp.  `xs` is the token's fp32 activation
-// vector (shared or global memory), `wrow` the router row (global).
-// `vec_ok`: the row and H allow 16-byte vector loads.  Result valid on all
-// lanes.
+// Segment `seg` partial sums of rows [0, E) of gate_w against the fp32 vector
+// xs (shared memory), computed by one warp.  Writes part[e] (lane 0) for
+// every row.  vec_ok: rows and H allow 16-byte vector loads.
 template <typename Tw>
-WR_DEVINL float router_logit_warp(const Tw* __restrict__ wrow, const float* __restrict__ xs,
-                                  int H, int lane, bool vec_ok) {
+WR_DEVINL void router_segment_warp(const Tw* __restrict__ gate_w, const float* __restrict__ xs,
+                                   int E, int H, int seg, int lane, bool vec_ok,
+                                   float* __restrict__ part) {
   constexpr int VEC = Chunk<Tw>::kVec;
-  float acc = 0.0f;
-  if (vec_ok) {
-    const int nvec = H / VEC;
-#pragma unroll 4
-    for (int v = lane; v < nvec; v += 32) {
-      const uint4 raw = ldg_nc_v4(wrow + (int64_t)v * VEC);
-      float f[VEC];
-      Chunk<Tw>::widen(raw, f);
-      const float* xv = xs + (int64_t)v * VEC;
+  constexpr int RB = kRouterRowBatch;
+  const int nvec = (H + VEC - 1) / VEC;
+  const int lo = (int)((int64_t)nvec * seg / kRouterSegments);
+  const int hi = (int)((int64_t)nvec * (seg + 1) / kRouterSegments);
+  for (int e0 = 0; e0 < E; e0 += RB) {
+    float acc[RB];
 #pragma unroll
-      for (int q = 0; q < VEC; ++q) acc = __fmaf_rn(f[q], xv[q], acc);
-    }
-  } else {
-    const int nvec = (H + VEC - 1) / VEC;
-    for (int v = lane; v < nvec; v += 32) {
+    for (int r = 0; r < RB; ++r) acc[r] = 0.0f;
+    if (vec_ok) {
+      for (int v = lo + lane; v < hi; v += 32) {
+        uint4 raw[RB];
 #pragma unroll
-      for (int q = 0; q < VEC; ++q) {
-        const int j = v * VEC + q;
-        if (j < H) acc = __fmaf_rn(load_scalar<Tw>(wrow, j), xs[j], acc);
+        for (int r = 0; r < RB; ++r)
+          if (e0 + r < E) raw[r] = ldg_nc_v4(gate_w + (int64_t)(e0 + r) * H + (int64_t)v * VEC);
+        const float* xv = xs + (int64_t)v * VEC;
+        float xf[VEC];
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) xf[q] = xv[q];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (e0 + r < E) {
+            float f[VEC];
+            Chunk<Tw>::widen(raw[r], f);
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[r] = __fmaf_rn(f[q], xf[q], acc[r]);
+          }
+        }
+      }
+    } else {
+      for (int v = lo + lane; v < hi; v += 32) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (e0 + r >= E) continue;
+          const Tw* row = gate_w + (int64_t)(e0 + r) * H;
+#pragma unroll
+          for (int q = 0; q < VEC; ++q) {
+            const int j = v * VEC + q;
+            if (j < H) acc[r] = __fmaf_rn(load_scalar<Tw>(row, j), xs[j], acc[r]);
+          }
+        }
       }
     }
-  }
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1)
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-  return acc;
+    for (int r = 0; r < RB; ++r) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+        acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], off));
+      if (lane == 0 && e0 + r < E) part[e0 + r] = acc[r];
+    }
+  }
 }
 
-// Softmax + top-K for one token, run by a single thread.
-// logits [E] (E <= 64) -> ids [K], weights [K] (probabilities of the picks).
-WR_DEVINL void softmax_topk(const float* logits, int E, int K, int* ids, float* weights) {
-  float m = logits[0];
-  for (int e = 1; e < E; ++e) m = fmaxf(m, logits[e]);
-  float s = 0.0f;
-  for (int e = 0; e < E; ++e) s = __fadd_rn(s, expf(logits[e] - m));
-  uint64_t used = 0;
+// logit = (((s_0 + s_1) + s_2) + ... + s_7) [+ bias]; parts laid out
+// [segment][stride] with the expert index as the fastest dimension.
+WR_DEVINL float router_combine(const float* parts, int stride, int e, const float* bias) {
+  float l = parts[e];
+#pragma unroll
+  for (int j = 1; j < kRouterSegments; ++j) l = __fadd_rn(l, parts[j * stride + e]);
+  if (bias) l = __fadd_rn(l, bias[e]);
+  return l;
+}
+
+// Softmax + top-K for one token, run by one full warp.
+// logits [E] (E <= 64, any memory) -> ids [K], weights [K] (written by lane 0).
+// Selection: K rounds of "largest key, lowest index on ties" over the unused
+// experts, key = logit (NaN counts as -inf) — warp-route's strict-'>'
+// argmax (src/fused_moe.cu:134-142) with ties to the lowest index.
+// Softmax: m = max logit; p_e = exp(l_e - m); the sum is a fixed tree —
+// lane l adds p_l + p_{l+32}, then a 16/8/4/2/1 xor tree; weight_k =
+// p_{id_k} / sum.
+WR_DEVINL void select_topk_warp(const float* logits, int E, int K, int lane, int* ids,
+                                float* weights) {
+  const float ninf = __int_as_float(0xff800000);
+  const int e0 = lane, e1 = lane + 32;
+  const float l0 = e0 < E ? logits[e0] : ninf;
+  const float l1 = e1 < E ? logits[e1] : ninf;
+  float m = fmaxf(l0, l1);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  const float p0 = e0 < E ? expf(l0 - m) : 0.0f;
+  const float p1 = e1 < E ? expf(l1 - m) : 0.0f;
+  float s = __fadd_rn(p0, p1);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  bool used0 = e0 >= E, used1 = e1 >= E;
   for (int k = 0; k < K; ++k) {
-    int best = -1;
-    for (int e = 0; e < E; ++e) {
-      if ((used >> e) & 1ull) continue;
-      if (best < 0 || logits[e] > logits[best]) best = e;
+    // this lane's best unused candidate
+    float kv = ninf;
+    int ki = 1 << 20;
+    if (!used0) { kv = (l0 != l0) ? ninf : l0; ki = e0; }
+    if (!used1) {
+      const float v1 = (l1 != l1) ? ninf : l1;
+      if (ki == (1 << 20) || v1 > kv) { kv = v1; ki = e1; }
     }
-    used |= 1ull << best;
-    ids[k] = best;
-    weights[k] = __fdiv_rn(expf(logits[best] - m), s);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, kv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, ki, off);
+      if (ov > kv || (ov == kv && oi < ki)) { kv = ov; ki = oi; }
+    }
+    if (ki == e0) used0 = true;
+    if (ki == e1) used1 = true;
+    // the lane holding expert ki (lane ki & 31) supplies its probability
+    const float pb = __shfl_sync(0xffffffffu, (ki == e0) ? p0 : p1, ki & 31);
+    if (lane == 0) {
+      ids[k] = ki;
+      weights[k] = __fdiv_rn(pb, s);
+    }
   }
 }
 
