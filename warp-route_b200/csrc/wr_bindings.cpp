@@ -30,18 +30,23 @@ namespace {
   TORCH_CHECK((t).scalar_type() == torch::kFloat32 || (t).scalar_type() == torch::kBFloat16, \
               #t " must be float32 or bfloat16")
 
+// warp-route's validate_1d/2d (src/bindings.cpp:13-23) stringify their own
+// parameter ("t must be ..."); these name the argument instead.
+void check_tensor(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.scalar_type() == torch::kFloat32 || t.scalar_type() == torch::kBFloat16, name,
+              " must be float32 or bfloat16");
+}
+
 void validate_1d(const torch::Tensor& t, const char* name, int64_t expected) {
-  CHECK_CUDA(t);
-  CHECK_CONTIGUOUS(t);
-  CHECK_DTYPE(t);
+  check_tensor(t, name);
   TORCH_CHECK(t.dim() == 1 && t.size(0) == expected, name, " must have shape [", expected,
               "], got shape ", t.sizes());
 }
 
 void validate_2d(const torch::Tensor& t, const char* name, int64_t rows, int64_t cols) {
-  CHECK_CUDA(t);
-  CHECK_CONTIGUOUS(t);
-  CHECK_DTYPE(t);
+  check_tensor(t, name);
   TORCH_CHECK(t.dim() == 2 && t.size(0) == rows && t.size(1) == cols, name,
               " must have shape [", rows, ", ", cols, "], got shape ", t.sizes());
 }
