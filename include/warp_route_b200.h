@@ -141,6 +141,23 @@ WR_API wr_status_t wr_fused_moe(const wr_moe_desc_t* desc, const void* x,
                          void* workspace, size_t workspace_bytes,
                          wr_stream_t stream);
 
+/* One decode token, exactly as wr_fused_moe, but with no workspace argument:
+ * for callers that cannot allocate device memory (a host that owns the whole
+ * device heap and gives the code it loads no workspace).  The scratch comes
+ * from a 1 MiB array built into the library, which every GPU that loads the
+ * library holds until the process exits; a layer that needs more (about
+ * top_k * intermediate_dim * 4 + 1280 bytes) gets WR_ERR_UNSUPPORTED and
+ * nothing is launched.  All calls on one device share the array and its
+ * control words are cleared on `stream` before each launch, so calls that
+ * overlap on the GPU race: serialise them.  The first call on each device
+ * looks up the array's device address; make that call before any stream
+ * capture.  No counterpart in warp-route. */
+WR_API wr_status_t wr_fused_moe_noalloc(const wr_moe_desc_t* desc, const void* x,
+                                        const void* gate_w, const void* weight_buf,
+                                        int64_t weight_buf_bytes, float* out,
+                                        int32_t* topk_ids, float* topk_weights,
+                                        wr_stream_t stream);
+
 /* ---- fused layer, a batch of tokens ----------------------------------- */
 
 /* num_tokens decode tokens: x [T,H] -> out [T,H] (fp32); topk_ids [T,K] and

@@ -61,6 +61,7 @@ SIGNATURES = {
     "wr_router_topk": (_i32, [_D, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "wr_fused_moe_workspace_size": (_sz, [_D, _i32]),
     "wr_fused_moe": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "wr_fused_moe_noalloc": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "wr_batched_fused_moe": (_i32, [_D, _i32, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "wr_naive_moe_workspace_size": (_sz, [_D]),
     "wr_naive_moe": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
