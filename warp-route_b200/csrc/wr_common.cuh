@@ -149,6 +149,16 @@ WR_DEVINL uint32_t ld_acquire_gpu(const uint32_t* p) {
 WR_DEVINL void red_release_gpu_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// The same at CTA scope on a shared-memory word.
+WR_DEVINL uint32_t ld_acquire_cta_smem(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+WR_DEVINL void red_release_cta_smem_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
+               : "memory");
+}
 
 // 16-byte read-only global load that does not allocate in L1.
 WR_DEVINL uint4 ldg_nc_v4(const void* p) {

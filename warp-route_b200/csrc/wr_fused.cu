@@ -16,33 +16,42 @@
 // k_fused_stream: one persistent CTA per SM (227 KB shared memory):
 //   warps 0-7  consumers: selection, then dot products out of shared memory;
 //   warp 8     producer: lane 0 issues cp.async.bulk copies into a ring of
-//              7-12 stages of ~16 KB (mbarrier full/empty pairs, L2
-//              evict-first) and never waits on the math.
-// Every copy is a contiguous run of weight rows (8-32 KB): B200's TMA
+//              5-12 stages of up to 32 KB (mbarrier full/empty pairs, L2
+//              evict-first) and never waits on the math;
+//   warp 9     publisher: signals grid-wide when this CTA's activations of a
+//              slot are complete (below).
+// Every copy is a contiguous run of weight rows (up to 32 KB): B200's TMA
 // streams at HBM bandwidth only with large contiguous copies.
 //
 // The selected experts become "slots"; the layer is then two matvecs:
 //   phase A  rows p = slot*I + i of [Wg; Wu] . x -> act[p] =
 //            w_slot * silu(g) * u (fp32 workspace, one value per token).
 //            A stage holds GA gate rows and the same GA up rows (two copies).
+//            Groups of GA row pairs are dealt to the CTAs round robin, slot
+//            after slot, so slot 0's activations are complete about halfway.
 //   phase B  out[h] = sum over slots of Wd_slot[h, :] . act[slot, :].  The
 //            slot's activations sit in shared memory in windows of at most
-//            16 KB of weight columns; a stage is GB rows of one window.
-// Each row is owned by one warp (row index mod 8) that computes its whole
-// dot product.  Only the owners of a stage wait for it, process it and
-// release it (the producer pre-arrives for the others), so the eight warps
-// work on eight different stages at once.  Because a warp skips the stages
-// it does not own, a parity wait alone could mistake a later use of the
-// ring slot for the one it wants; the producer therefore tags each slot
-// with the number of the stage it holds, and an owner waits for its tag
-// before its parity wait (the tag is written only after the slot's previous
-// use was released, so the parity is then unambiguous).  No partial sum crosses a
-// warp, so results are deterministic (fixed lane order and trees, fixed
-// slot/window order, no floating-point atomics).  Phase A rows and phase B
-// rows are split evenly over the CTAs, each CTA starting at a rotated
-// position of its range (spreads DRAM channels).  One grid-wide barrier
-// (bounded spin) separates the phases; the producer keeps prefetching
-// phase-B weights across it.
+//            16384 columns; a stage is GB rows of one window.  Output rows
+//            are split evenly over the CTAs.
+// Phase A rows are owned by one warp each (the CTA's k-th row pair by warp
+// k % 8), which computes the whole dot product.  Phase B rows are read by
+// PB warps (1 or 2), each taking a column slice; every warp adds into its
+// own row accumulators, summed in warp order at the end.  Only the warps
+// that read a stage wait for it and release it (the producer pre-arrives
+// for the others), so the warps work on different stages at once.  Because
+// a warp skips the stages it does not read, a parity wait alone could
+// mistake a later use of the ring slot for the one it wants; the producer
+// therefore tags each slot with the number of the stage it holds, and a
+// reader waits for its tag before its parity wait (the tag is written only
+// after the slot's previous use was released, so the parity is then
+// unambiguous).  No partial sum crosses a warp except in the fixed final
+// sum, so results are deterministic (fixed lane order and trees, fixed
+// slot/window order, no floating-point atomics).
+// Completion of slot s: each consumer warp arrives on a per-slot mbarrier
+// once its share of slot s is written; the publisher warp waits on it and
+// adds the CTA to the grid-wide counter of slot s with one GPU-scope
+// release.  Phase B of slot s starts once that counter holds every CTA
+// (bounded spin); the producer keeps prefetching phase-B weights meanwhile.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -56,8 +65,8 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + producer warp
-constexpr int kTargetStage = 16 * 1024;          // stage size aimed for
+constexpr int kThreads = kConsumerThreads + 64;  // + producer warp + publisher warp
+constexpr int kTargetStage = 32 * 1024;          // stage size aimed for
 constexpr int kMaxStageBytes = 32 * 1024;
 constexpr int kMaxStages = 12;
 constexpr int kSmemBytes = 232448;  // 227 KB: the sm_100 per-CTA opt-in maximum
@@ -79,16 +88,17 @@ constexpr int kOffSlotE = 512;     // int [64]: local expert of each slot
 constexpr int kOffSlotW = 768;     // float [64 * NT]: routing weight (0: not routed)
 constexpr int kOffTokIds = 1792;   // int [NT * 64]
 constexpr int kOffTokW = 2816;     // float [NT * 64]
-constexpr int kOffRowAcc = 3840;   // float [rows * NT]: phase-B row accumulators
-constexpr int kRowAccFloats = (kMiscBytes - kOffRowAcc) / 4;
+constexpr int kOffSlotBar = 3840;  // mbarrier [64]: the W consumer warps are done with slot s
 static_assert(kOffBars + 8 * (2 * kMaxStages + 1) <= kOffAbort, "misc");
-static_assert(kRowAccFloats >= 1024, "misc");
+static_assert(kOffTokW + 4 * kMaxNT * kMaxExperts <= kOffSlotBar, "misc");
+static_assert(kOffSlotBar + 8 * kMaxExperts <= kMiscBytes, "misc");
 
 // Workspace: control words, router logits, activations.
-constexpr int kSyncArrive = 0;
-constexpr int kSyncExit = 1;
-constexpr int kSyncStatus = 2;
-constexpr size_t kSyncBytes = 256;
+constexpr int kSyncExit = 1;      // CTAs that have finished (self-reset)
+constexpr int kSyncStatus = 2;    // DEV_TIMEOUT_* bits
+constexpr int kSyncSlot0 = 64;    // [64 + s]: CTAs whose slot-s activations are all written
+constexpr size_t kSyncBytes = kWsControlBytes;
+static_assert((kSyncSlot0 + kMaxExperts) * 4 <= (int)kSyncBytes, "control words");
 constexpr size_t kLogitBytes = (size_t)kMaxNT * kMaxExperts * 4;  // 1 KB
 constexpr size_t kActOffset = kSyncBytes + kLogitBytes;
 
@@ -104,6 +114,10 @@ struct Plan {
   int GB;    // phase B: rows per stage
   int SB;    // stage bytes
   int nst;   // ring stages
+  int PB;      // phase B: warps per row, each taking a column slice (1, 2, 4 or 8)
+  int orderA;  // phase A group order (kOrderRoundRobin / kOrderRanges)
+  int NBM;     // phase B: most output rows one CTA holds
+  int RA;      // float offset of the per-warp row accumulators [W][NBM][NT] in the vector region
 };
 
 struct FusedArgs {
@@ -209,17 +223,17 @@ WR_DEVINL void dot_pair(const uint4* __restrict__ gp, const uint4* __restrict__ 
   }
 }
 
-// Phase B dot of one down-row piece over chunks [0, nch) against the
-// activation window (layout [column][NT]).
+// Phase B dot of one down-row piece over chunks j0, j0 + js, ... < nch
+// against the activation window (layout [column][NT]).
 template <typename Tw, int NT>
 WR_DEVINL void dot_down(const uint4* __restrict__ wp, const float* __restrict__ av, int nch,
-                        int lane, float (&acc)[NT]) {
+                        int j0, int js, float (&acc)[NT]) {
   constexpr int VEC = Chunk<Tw>::kVec;
   float acc1[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc1[t] = 0.0f;
 #pragma unroll 4
-  for (int j = lane; j < nch; j += 32) {
+  for (int j = j0; j < nch; j += js) {
     float wf[VEC];
     Chunk<Tw>::widen(wp[j], wf);
     const float4* a4p = reinterpret_cast<const float4*>(av + j * VEC * NT);
@@ -261,45 +275,88 @@ struct Cursor {
   }
 };
 
-// Phase A row groups of one CTA, in its rotated order: groups of up to GA
-// consecutive row pairs of one slot, over the CTA's rows [pa0, pa1).
-struct UnitsA {
-  int pa0, pa1, I, GA;
-  int s, r, hi;  // current group: rows [r, min(r + GA, hi)) of slot s
-  WR_DEVINL void seg(int slot) {
-    s = slot;
-    r = max(pa0, s * I);
-    hi = min(pa1, (s + 1) * I);
+// Phase A work of one CTA.  Each slot's I row pairs form ng groups of GA
+// consecutive row pairs.  Every CTA finishes its share of slot s before it
+// starts slot s + 1, so slot s's activations are complete early.  Two orders:
+//   kOrderRoundRobin  the S * ng groups, slot after slot, dealt round robin
+//                     (group q to CTA q mod G): the grid sweeps one
+//                     contiguous window of the weights;
+//   kOrderRanges      in slot s the CTA takes range number (b + 53 s) mod G of
+//                     G near-equal contiguous ranges, from a rotated start;
+//   kOrderGlobal      one contiguous range of the slot-major list, from a
+//                     rotated start (slots are then published only at the end).
+enum { kOrderRoundRobin = 0, kOrderRanges = 1, kOrderGlobal = 2 };
+// Advanced one group at a time without divisions (except once per slot
+// range or wrap), since every consumer warp and the producer step it for
+// every stage.
+struct GroupsA {
+  int mode, b, G, S, ng, GA, I;
+  int k, n, lo, rot;  // position k of n in the current range starting at group lo
+  int s, j;           // current group: number j of slot s
+  int r, g;           // its row pairs [r, r + g)
+  WR_DEVINL void set() {
+    r = j * GA;
+    g = min(GA, I - r);
   }
-  // Places the cursor on group number `u` of the natural order.
-  WR_DEVINL void init(int pa0_, int pa1_, int I_, int GA_, int u) {
-    pa0 = pa0_; pa1 = pa1_; I = I_; GA = GA_;
-    seg(pa0 / I);
-    for (;;) {
-      const int n = (hi - r + GA - 1) / GA;
-      if (u < n || n <= 0) { r += u * GA; return; }
-      u -= n;
-      seg(s + 1);
+  // kOrderRanges: the first slot >= `slot` in which this CTA has groups.
+  WR_DEVINL void range(int slot) {
+    for (s = slot; s < S; ++s) {
+      const int c = (int)((b + 53LL * s) % G);
+      lo = (int)((int64_t)ng * c / G);
+      n = (int)((int64_t)ng * (c + 1) / G) - lo;
+      if (n > 0) break;
+    }
+    k = 0;
+    rot = n > 0 ? (int)(((int64_t)b * 37) % n) : 0;
+    j = lo + rot;
+    if (s < S) set();
+  }
+  // kOrderGlobal: position on global group number q.
+  WR_DEVINL void at(int q) {
+    s = q / ng;
+    j = q - s * ng;
+    set();
+  }
+  WR_DEVINL void init(int mode_, int b_, int G_, int S_, int ng_, int GA_, int I_) {
+    mode = mode_; b = b_; G = G_; S = S_; ng = ng_; GA = GA_; I = I_;
+    if (mode == kOrderRanges) {
+      range(0);
+    } else if (mode == kOrderGlobal) {
+      const int64_t Q = (int64_t)S * ng;
+      lo = (int)(Q * b / G);
+      n = (int)(Q * (b + 1) / G) - lo;
+      rot = n > 0 ? (int)(((int64_t)b * 37) % n) : 0;
+      k = 0;
+      if (n > 0) at(lo + rot); else s = S;
+    } else {
+      if ((int64_t)b < (int64_t)S * ng) at(b); else s = S;
     }
   }
-  WR_DEVINL int g() const { return min(GA, hi - r); }
+  WR_DEVINL bool valid() const { return s < S; }
   WR_DEVINL void next() {
-    r += GA;
-    if (r >= hi) {
-      if (hi >= pa1) seg(pa0 / I);  // wrap to the start of the range
-      else seg(s + 1);
+    if (mode == kOrderRanges) {
+      if (++k == n) {
+        range(s + 1);
+      } else {
+        if (++j == lo + n) j = lo;
+        set();
+      }
+    } else if (mode == kOrderGlobal) {
+      if (++k == n) {
+        s = S;
+      } else if (k == n - rot) {
+        at(lo);  // wrap to the start of the range
+      } else {
+        if (++j == ng) { j = 0; ++s; }
+        set();
+      }
+    } else {
+      j += G;
+      while (j >= ng && s < S) { j -= ng; ++s; }
+      if (s < S) set();
     }
   }
 };
-
-WR_DEVINL int count_units_a(int pa0, int pa1, int I, int GA) {
-  int n = 0;
-  for (int s = pa0 / I; s * I < pa1; ++s) {
-    const int lo = max(pa0, s * I), hi = min(pa1, (s + 1) * I);
-    n += (hi - lo + GA - 1) / GA;
-  }
-  return n;
-}
 
 template <typename Tw, int NT>
 __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a) {
@@ -323,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   float* slot_w = reinterpret_cast<float*>(misc + kOffSlotW);
   int* tok_ids = reinterpret_cast<int*>(misc + kOffTokIds);
   float* tok_w = reinterpret_cast<float*>(misc + kOffTokW);
-  float* rowacc = reinterpret_cast<float*>(misc + kOffRowAcc);
+  float* rowacc = vreg + pl.RA;  // [W][NBM][NT] phase-B partial sums, one set per warp
+  uint64_t* slot_bar = reinterpret_cast<uint64_t*>(misc + kOffSlotBar);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -332,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   const int G = gridDim.x, b = blockIdx.x;
 
   if (tid == 0) {
+    for (int s = 0; s < kMaxExperts; ++s) mbar_init(&slot_bar[s], W);
     for (int s = 0; s < nst; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], W);
@@ -398,12 +457,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   __syncthreads();
 
   const int S = *s_nslots;
-  const int P = S * I;  // phase A rows (S <= 64, I < 2^25)
-  const int pa0 = (int)split_lo(P, b, G), pa1 = (int)split_lo(P, b + 1, G);
+  const int ng = (I + pl.GA - 1) / pl.GA;  // phase A groups per slot (S * I < 2^30)
   const int hb0 = (int)split_lo(H, b, G), hb1 = (int)split_lo(H, b + 1, G);
   const int nb = hb1 - hb0;
-  const int na_u = pa1 > pa0 ? count_units_a(pa0, pa1, I, pl.GA) : 0;
-  const int rot_a = na_u ? (int)(((int64_t)b * 37) % na_u) : 0;
   const int nb_u = (nb + pl.GB - 1) / pl.GB;
   const int hb_start = hb0 + (nb_u ? (int)(((int64_t)b * 11) % nb_u) : 0) * pl.GB;
   const int wc_last = I - (pl.nwin - 1) * pl.WB;  // width of a slot's last window
@@ -429,21 +485,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         slot_tag[c.si] = issued;
         return true;
       };
-      // Owners of rows [base, base + g) (mod W) release the stage; arrive
-      // for the other warps now.
-      auto commit = [&](int g) {
-        const int owners = g < W ? g : W;
+      // `owners` warps will release the stage; arrive for the others now.
+      auto commit = [&](int owners) {
         if (owners < W) mbar_arrive_cnt(&empty[c.si], (uint32_t)(W - owners));
         c.next(nst);
         ++issued;
       };
       // phase A
-      UnitsA u;
-      u.init(pa0, pa1, I, pl.GA, rot_a);
-      for (int uu = 0; uu < na_u && ok; ++uu, u.next()) {
-        const int g = u.g();
-        const uint8_t* eb = a.wbuf + (int64_t)slot_e[u.s] * a.lay.stride +
-                            (int64_t)(u.r - u.s * I) * H * ELT;
+      GroupsA ga;
+      ga.init(pl.orderA, b, G, S, ng, pl.GA, I);
+      for (; ga.valid() && ok; ga.next()) {
+        const int g = ga.g;
+        const uint8_t* eb =
+            a.wbuf + (int64_t)slot_e[ga.s] * a.lay.stride + (int64_t)ga.r * H * ELT;
         for (int c0 = 0; c0 < H; c0 += pl.CWA) {
           if (!(ok = reserve())) break;
           const int cw = min(pl.CWA, H - c0);
@@ -453,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           const uint8_t* src = eb + (int64_t)c0 * ELT;
           bulk_g2s(st, src + a.lay.off_gate, piece, &full[c.si], pol);
           bulk_g2s(st + pl.GA * pl.CWA * ELT, src + a.lay.off_up, piece, &full[c.si], pol);
-          commit(g);
+          commit(g < W ? g : W);
         }
       }
       // phase B
@@ -475,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
                 bulk_g2s(st + r * pl.WB * ELT, src + (int64_t)r * I * ELT, wc * ELT, &full[c.si],
                          pol);
             }
-            commit(g);
+            commit(min(g, W / pl.PB) * pl.PB);
             hb += pl.GB;
             if (hb >= hb1) hb = hb0;
           }
@@ -489,6 +543,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           if (!mbar_wait(&full[j % nst], (uint32_t)(j / nst) & 1u, nullptr))
             atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
         atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_EMPTY);
+      }
+    }
+  } else if (warp == W + 1) {
+    // =========================== publisher ==================================
+    // Once all W consumer warps of this CTA have written their slot-s
+    // activations (each arrives on slot_bar[s], used once per launch), counts
+    // the CTA in on the grid-wide counter of slot s with one GPU-scope
+    // release, so the consumers never stall on a GPU-scope release.
+    if (lane == 0) {
+      for (int s = 0; s < S; ++s) {
+        if (!mbar_wait(&slot_bar[s], 0u, abort_flag)) {
+          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
+          *abort_flag = 1;
+          break;
+        }
+        fence_proxy_async_global();
+        red_release_gpu_add(&a.sync[kSyncSlot0 + s], 1u);
       }
     }
   } else {
@@ -516,18 +587,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       return __all_sync(0xffffffffu, got);
     };
 
-    // ---- phase A: gate/up rows -> activations; row pair p owned by warp p%8 ----
+    // This warp's activations of slot s are written: tell the publisher.
+    auto publish = [&](int s) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&slot_bar[s]);
+    };
+
+    // ---- phase A: gate/up rows -> activations; the CTA's k-th row pair is
+    // owned by warp k % 8 ----
     {
       const int nch_full = pl.CWA / VEC;
       float ga[NT], ua[NT];  // running sums of a row pair split over stages
 #pragma unroll
       for (int t = 0; t < NT; ++t) ga[t] = ua[t] = 0.0f;
-      UnitsA u;
-      u.init(pa0, pa1, I, pl.GA, rot_a);
-      for (int uu = 0; uu < na_u; ++uu, u.next()) {
-        const int g = u.g();
-        const int first = (warp - (u.r & (W - 1)) + W) & (W - 1);  // my first row of the group
+      GroupsA gr;
+      gr.init(pl.orderA, b, G, S, ng, pl.GA, I);
+      int lrow = 0;      // row pairs of this CTA before the current group
+      int published = 0; // slots [0, published) are published by this warp
+      for (; gr.valid(); gr.next()) {
+        if (pl.orderA != kOrderGlobal)
+          for (; published < gr.s; ++published) publish(published);
+        const int g = gr.g;
+        const int p0 = gr.s * I + gr.r;  // activation row of the group's first row pair
+        const int first = (warp - (lrow & (W - 1)) + W) & (W - 1);  // my first row of the group
         const bool mine = first < g;
+        lrow += g;
         for (int c0 = 0; c0 < H; c0 += pl.CWA) {
           const int cw = min(pl.CWA, H - c0);
           if (ok && mine) ok = wait_owned();
@@ -557,8 +641,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 #pragma unroll
                   for (int t = 0; t < NT; ++t) {
                     if (lane == t) {
-                      const float wt = slot_w[u.s * NT + t];
-                      a.act[((int64_t)u.r + rr) * NT + t] =
+                      const float wt = slot_w[gr.s * NT + t];
+                      a.act[((int64_t)p0 + rr) * NT + t] =
                           (wt != 0.0f) ? wt * (silu(gg[k][t]) * uv[k][t]) : 0.0f;
                     }
                   }
@@ -577,8 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                   if (lane == t) {
-                    const float wt = slot_w[u.s * NT + t];
-                    a.act[(int64_t)u.r * NT + t] = (wt != 0.0f) ? wt * (silu(ga[t]) * ua[t]) : 0.0f;
+                    const float wt = slot_w[gr.s * NT + t];
+                    a.act[(int64_t)p0 * NT + t] = (wt != 0.0f) ? wt * (silu(ga[t]) * ua[t]) : 0.0f;
                   }
                 }
 #pragma unroll
@@ -590,32 +674,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           ++stage;
         }
       }
+      for (; published < S; ++published) publish(published);
     }
     if (!ok && lane == 0) *abort_flag = 1;
-    for (int i = tid; i < nb * NT; i += kConsumerThreads) rowacc[i] = 0.0f;
+    for (int i = tid; i < W * pl.NBM * NT; i += kConsumerThreads) rowacc[i] = 0.0f;
 
-    // ---- grid-wide barrier: every CTA's activations are written ----
-    named_bar_sync(kBarConsumers, kConsumerThreads);
-    if (tid == 0) {
-      __threadfence();
-      fence_proxy_async_global();
-      red_release_gpu_add(&a.sync[kSyncArrive], 1u);
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t spins = 0;
-      while (ld_acquire_gpu(&a.sync[kSyncArrive]) < (uint32_t)G) {
-        if ((++spins & 63u) == 0) {
-          if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
-            *abort_flag = 1;
-            break;
-          }
-        }
-      }
-      fence_proxy_async_global();
-    }
-
-    // ---- phase B: down rows, slot by slot; local row h owned by warp h%8 ----
+    // ---- phase B: down rows, slot by slot.  Each row is read by PB warps,
+    // each taking a column slice; warp w adds into its own accumulators
+    // rowacc[w][h][t], summed in warp order at the end. ----
     {
+      const uint32_t slot_target = (uint32_t)G;
+      const int GW = W / pl.PB;         // row groups of PB warps
+      const int partB = warp % pl.PB;   // my column slice
+      const int grpB = warp / pl.PB;    // my row group
       uint32_t aw = 0;
       int act_issued = 0;
       for (int s = 0; s < S; ++s) {
@@ -624,6 +695,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           const int nch = wc / VEC;
           named_bar_sync(kBarConsumers, kConsumerThreads);  // previous window fully read
           if (*abort_flag) ok = false;
+          if (tid == 0 && ok && win == 0) {
+            // Every CTA has published slot s.
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(&a.sync[kSyncSlot0 + s]) < slot_target) {
+              if ((++spins & 63u) == 0 &&
+                  (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
+                atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+            }
+            fence_proxy_async_global();
+          }
           if (tid == 0 && ok) {
             fence_proxy_async_smem();
             const uint32_t bytes = (uint32_t)wc * NT * 4;
@@ -641,7 +727,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           int hb = hb_start;
           for (int uu = 0; uu < nb_u; ++uu) {
             const int g = min(pl.GB, hb1 - hb);
-            const int first = (warp - ((hb - hb0) & (W - 1)) + W) & (W - 1);
+            // local row lr is read by the PB warps of row group lr % GW, warp
+            // `part` of them taking chunks part*32 + lane + PB*32*k
+            const int lr0 = hb - hb0;  // local row of the stage's first row
+            const int first = (grpB - (lr0 & (GW - 1)) + GW) & (GW - 1);  // my first row of it
+            float* racc = rowacc + ((int64_t)warp * pl.NBM + lr0) * NT;
             if (ok && first < g) ok = wait_owned();
             if (ok && first < g) {
               const uint8_t* st = ring + c.si * pl.SB;
@@ -650,21 +740,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
               for (int k = 0; k < kRowsPerWarp; ++k) {
 #pragma unroll
                 for (int t = 0; t < NT; ++t) v[k][t] = 0.0f;
-                const int rr = first + k * W;
+                const int rr = first + k * GW;
                 if (rr < g)
                   dot_down<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.WB * ELT), vreg, nch,
-                                   lane, v[k]);
+                                   partB * 32 + lane, pl.PB * 32, v[k]);
               }
               __syncwarp();
               if (lane == 0) mbar_arrive(&empty[c.si]);
 #pragma unroll
               for (int k = 0; k < kRowsPerWarp; ++k) {
-                const int rr = first + k * W;
+                const int rr = first + k * GW;
                 if (rr < g) {
                   warp_sum<NT>(v[k]);
                   if (lane == 0) {
 #pragma unroll
-                    for (int t = 0; t < NT; ++t) rowacc[(hb - hb0 + rr) * NT + t] += v[k][t];
+                    for (int t = 0; t < NT; ++t) racc[rr * NT + t] += v[k][t];
                   }
                 }
               }
@@ -682,7 +772,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         for (int idx = tid; idx < T * nb; idx += kConsumerThreads) {
           const int t = idx / nb;
           const int h = idx - t * nb;
-          a.out[(int64_t)t * H + hb0 + h] = rowacc[h * NT + t];
+          float o = rowacc[h * NT + t];
+#pragma unroll
+          for (int w = 1; w < W; ++w) o += rowacc[((int64_t)w * pl.NBM + h) * NT + t];
+          a.out[(int64_t)t * H + hb0 + h] = o;
         }
       }
       if (tid == 0 && act_issued > 0 && !ok) {
@@ -696,12 +789,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 
   __syncthreads();
   if (tid == 0) {
-    // Self-reset of the grid barrier: every CTA has left its wait once it
-    // counts itself out, so the last one can clear both counters.
+    // Self-reset of the slot counters: every CTA has left its waits once it
+    // counts itself out, so the last one can clear them all.
     __threadfence();
     const uint32_t prev = atomicAdd(&a.sync[kSyncExit], 1u);
     if (prev == (uint32_t)G - 1) {
-      atomicExch(&a.sync[kSyncArrive], 0u);
+      for (int s = 0; s < S; ++s) atomicExch(&a.sync[kSyncSlot0 + s], 0u);
       atomicExch(&a.sync[kSyncExit], 0u);
       __threadfence();
     }
@@ -777,10 +870,11 @@ int clamp_rows(int64_t g) {
   return (int)(g > kMaxRowsPerStage ? kMaxRowsPerStage : g);
 }
 
-Plan make_plan(const Problem& p, int nt) {
+Plan make_plan(const Problem& p, int nt, int grid) {
   const int elt = p.elt, vec = 16 / elt;
   Plan pl;
-  // phase A: whole row pairs when one fits in a stage, else 16 KB pieces
+  // phase A: whole row pairs when one fits in a stage, else pieces of
+  // kTargetStage / 2 bytes of one gate row and one up row
   const int64_t pair = 2LL * p.H * elt;
   int stage_a;
   if (pair <= kMaxStageBytes) {
@@ -809,11 +903,20 @@ Plan make_plan(const Problem& p, int nt) {
   sb = (sb + 127) / 128 * 128;
   pl.GB = clamp_rows(sb / row_b);
   pl.SB = sb;
+  // Long rows are split by columns over PB warps (shorter holds of each
+  // stage); a warp then reads at most kRowsPerWarp rows of a stage.
+  const int nchB = pl.WB / vec;
+  pl.PB = nchB >= 1536 ? 2 : 1;
+  while (pl.PB > 1 && pl.GB > kRowsPerWarp * (kConsumerWarps / pl.PB)) pl.PB /= 2;
+  pl.orderA = kOrderRoundRobin;
+  pl.NBM = (p.H + grid - 1) / grid;
   int64_t need = (int64_t)nt * p.H * 4;
   if ((int64_t)pl.WB * nt * 4 > need) need = (int64_t)pl.WB * nt * 4;
   need = (need + 63) / 64 * 64;
-  int nst = (int)((kMiscOff - need) / sb);
-  pl.nst = nst > kMaxStages ? kMaxStages : nst;
+  pl.RA = (int)(need / 4);
+  need += ((int64_t)kConsumerWarps * pl.NBM * nt * 4 + 63) / 64 * 64;
+  const int64_t nst = need < kMiscOff ? (kMiscOff - need) / sb : 0;
+  pl.nst = (int)(nst > kMaxStages ? kMaxStages : nst);
   return pl;
 }
 
@@ -827,10 +930,9 @@ bool fused_supported(const Problem& p) {
   const int nt = nt_bucket(p.T);
   if ((int64_t)nt * p.H * 4 > kVecMaxBytes) return false;  // x must fit in shared memory
   if ((int64_t)p.K * nt * p.I >= (1LL << 30)) return false; // 32-bit row indices
-  const int grid = device_sm_count();
-  const int64_t rows = ((int64_t)p.H + grid - 1) / grid;
-  if (rows * nt > kRowAccFloats) return false;             // phase-B row accumulators
-  return true;
+  // x (or an activation window) and the per-warp row accumulators must leave
+  // room for a ring of at least two stages
+  return make_plan(p, nt, device_sm_count()).nst >= 2;
 }
 
 size_t fused_workspace_bytes(const Problem& p) {
@@ -861,8 +963,8 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
   args.ep_num = p.ep_num;
   args.lay = make_layout(p.H, p.I, p.elt);
   const int nt = nt_bucket(p.T);
-  args.pl = make_plan(p, nt);
   const int grid = device_sm_count();
+  args.pl = make_plan(p, nt, grid);
   const float* bias = p.router_bias;
   if (p.dtype == WR_DTYPE_BF16) {
     if (nt == 1) return launch_pair<uint16_t, 1>(args, x, gate_w, bias, logits, grid, stream);

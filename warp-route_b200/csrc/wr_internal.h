@@ -9,6 +9,12 @@
 
 namespace wr {
 
+// Bytes at the start of every workspace reserved for the fused kernel's
+// control words (per-slot completion counters, exit counter, status word):
+// zero before the first call, left zero by every call.  The naive path keeps
+// its scratch behind them so both can share one workspace.
+constexpr size_t kWsControlBytes = 512;
+
 // Per-call problem description after validation.
 struct Problem {
   int E, H, I, K, T;          // experts, hidden, intermediate, top_k, tokens

@@ -145,10 +145,9 @@ struct NaiveScratch {
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// The first 256 bytes of every workspace hold the streaming kernel's
-// grid-barrier and status words; the naive path leaves them alone so one
-// workspace can serve both paths.
-constexpr size_t kWsReserved = 256;
+// The start of every workspace holds the streaming kernel's control words;
+// the naive path leaves them alone so one workspace can serve both paths.
+constexpr size_t kWsReserved = kWsControlBytes;
 
 NaiveScratch carve(const Problem& p, void* ws) {
   uint8_t* b = static_cast<uint8_t*>(ws) + kWsReserved;
