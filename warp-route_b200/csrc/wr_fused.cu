@@ -6,15 +6,15 @@
 // router -> top-K -> SwiGLU over the selected experts -> weighted combine,
 // spread over every SM instead of one warp.
 //
-// Two kernels per layer on one stream:
-//   k_router_logits  one CTA per (8 experts, token): every logit computed
-//                    once, written to the workspace.  It triggers the
-//                    dependent launch at once, so
-//   k_fused_stream   (programmatic dependent launch) is already resident,
-//                    has its barriers set up and x in shared memory, when
-//                    griddepcontrol.wait releases it.
-// k_fused_stream: one persistent CTA per SM (227 KB shared memory):
-//   warps 0-7  consumers: selection, then dot products out of shared memory;
+// One kernel per layer, k_fused_stream: one persistent CTA per SM (227 KB
+// shared memory), launched cooperatively with programmatic dependent launch:
+// it waits (griddepcontrol.wait) for the previous kernel on the stream, then
+// lets the next one start launching, so back-to-back layers do not pay a
+// full launch gap.
+//   router   every warp of the grid takes (token, 8-row batch, segment)
+//            items of the router sums; one grid-wide counter, then each CTA
+//            adds the 8 segment sums of every logit in order and selects;
+//   warps 0-7  consumers: dot products out of shared memory;
 //   warp 8     producer: lane 0 issues cp.async.bulk copies into a ring of
 //              5-12 stages of up to 32 KB (mbarrier full/empty pairs, L2
 //              evict-first) and never waits on the math;
@@ -89,18 +89,22 @@ constexpr int kOffSlotW = 768;     // float [64 * NT]: routing weight (0: not ro
 constexpr int kOffTokIds = 1792;   // int [NT * 64]
 constexpr int kOffTokW = 2816;     // float [NT * 64]
 constexpr int kOffSlotBar = 3840;  // mbarrier [64]: the W consumer warps are done with slot s
+constexpr int kOffLogits = 4352;   // float [NT * 64]: router logits
 static_assert(kOffBars + 8 * (2 * kMaxStages + 1) <= kOffAbort, "misc");
 static_assert(kOffTokW + 4 * kMaxNT * kMaxExperts <= kOffSlotBar, "misc");
-static_assert(kOffSlotBar + 8 * kMaxExperts <= kMiscBytes, "misc");
+static_assert(kOffSlotBar + 8 * kMaxExperts <= kOffLogits, "misc");
+static_assert(kOffLogits + 4 * kMaxNT * kMaxExperts <= kMiscBytes, "misc");
 
-// Workspace: control words, router logits, activations.
+// Workspace: control words, router partial sums, activations.
 constexpr int kSyncExit = 1;      // CTAs that have finished (self-reset)
 constexpr int kSyncStatus = 2;    // DEV_TIMEOUT_* bits
+constexpr int kSyncRouter = 3;    // CTAs whose router partial sums are written
 constexpr int kSyncSlot0 = 64;    // [64 + s]: CTAs whose slot-s activations are all written
 constexpr size_t kSyncBytes = kWsControlBytes;
 static_assert((kSyncSlot0 + kMaxExperts) * 4 <= (int)kSyncBytes, "control words");
-constexpr size_t kLogitBytes = (size_t)kMaxNT * kMaxExperts * 4;  // 1 KB
-constexpr size_t kActOffset = kSyncBytes + kLogitBytes;
+// router partial sums [T][segment][E] fp32
+constexpr size_t kRouterBytes = (size_t)kMaxNT * kRouterSegments * kMaxExperts * 4;  // 8 KB
+constexpr size_t kActOffset = kSyncBytes + kRouterBytes;
 
 // Named barrier 1: the eight consumer warps.
 constexpr int kBarConsumers = 1;
@@ -116,6 +120,7 @@ struct Plan {
   int nst;   // ring stages
   int PB;      // phase B: warps per row, each taking a column slice (1, 2, 4 or 8)
   int orderA;  // phase A group order (kOrderRoundRobin / kOrderRanges)
+  int localR;  // router: every CTA computes all partial sums itself (small routers)
   int NBM;     // phase B: most output rows one CTA holds
   int RA;      // float offset of the per-warp row accumulators [W][NBM][NT] in the vector region
 };
@@ -126,7 +131,9 @@ struct FusedArgs {
   float* out;
   int32_t* ids_out;
   float* w_out;
-  const float* logits;  // [T][E] from k_router_logits
+  const void* gate_w;   // [E][H]
+  const float* bias;    // [E] or null
+  float* rparts;        // [T][kRouterSegments][E] router partial sums (workspace)
   float* act;
   uint32_t* sync;
   int E, H, I, K, T;
@@ -140,46 +147,6 @@ WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts
 WR_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 WR_DEVINL void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// ---------------------------------------------------------------------------
-// Router logits: grid (ceil(E/8), T), 256 threads.  Warp j computes segment j
-// of 8 router rows; the 8 segment sums are added in order (the order of
-// wr_router.cuh, shared with k_router and the CPU oracle).
-// ---------------------------------------------------------------------------
-template <typename Tw>
-__global__ void __launch_bounds__(kConsumerThreads) k_router_logits(const Tw* __restrict__ x,
-                                                                    const Tw* __restrict__ gate_w,
-                                                                    const float* __restrict__ bias,
-                                                                    int E, int H,
-                                                                    float* __restrict__ logits) {
-  griddep_launch_dependents();
-  extern __shared__ __align__(16) float xs[];
-  __shared__ float parts[kRouterSegments * 8];
-  const int t = blockIdx.y;
-  const int e0 = blockIdx.x * 8;
-  const int nr = min(8, E - e0);
-  constexpr int VEC = Chunk<Tw>::kVec;
-  const Tw* xt = x + (int64_t)t * H;
-  for (int v = threadIdx.x; v < H / VEC; v += blockDim.x) {
-    float f[VEC];
-    Chunk<Tw>::widen(ldg_nc_v4(xt + (int64_t)v * VEC), f);
-#pragma unroll
-    for (int q = 0; q < VEC; ++q) xs[v * VEC + q] = f[q];
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  router_segment_warp<Tw>(gate_w + (int64_t)e0 * H, xs, nr, H, warp, lane, true,
-                          parts + warp * 8);
-  __syncthreads();
-  if (threadIdx.x < nr) {
-    const int r = threadIdx.x;
-    float l = parts[r];
-#pragma unroll
-    for (int j = 1; j < kRouterSegments; ++j) l = __fadd_rn(l, parts[j * 8 + r]);
-    if (bias) l = __fadd_rn(l, bias[e0 + r]);
-    logits[(int64_t)t * E + e0 + r] = l;
-  }
 }
 
 // Phase A dot products of one gate row and one up row over chunks [j0, j1)
@@ -380,6 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   float* slot_w = reinterpret_cast<float*>(misc + kOffSlotW);
   int* tok_ids = reinterpret_cast<int*>(misc + kOffTokIds);
   float* tok_w = reinterpret_cast<float*>(misc + kOffTokW);
+  float* s_logits = reinterpret_cast<float*>(misc + kOffLogits);
   float* rowacc = vreg + pl.RA;  // [W][NBM][NT] phase-B partial sums, one set per warp
   uint64_t* slot_bar = reinterpret_cast<uint64_t*>(misc + kOffSlotBar);
 
@@ -401,11 +369,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     fence_mbar_init();
   }
 
-  // ---- x -> shared memory as fp32 [NT][H] (tokens >= T are zero) ----------
-  {
+  // The previous kernel on the stream (which may have produced x, or be the
+  // previous call on this workspace) is complete from here on.  The next
+  // kernel may begin its launch now: its CTAs take over SMs as ours exit.
+  griddep_wait();
+  griddep_launch_dependents();
+
+  // ---- x -> shared memory as fp32 [NT][H] (tokens >= T are zero), by the
+  // producer and publisher warps, while the consumer warps compute the router
+  // partial sums: item (token t, row batch eb, segment seg) is segment seg of
+  // router rows [8 eb, 8 eb + 8) against x_t (the fixed order of
+  // wr_router.cuh).  Small routers (pl.localR) are computed whole by every
+  // CTA into shared memory (the ring is idle until the selection); larger
+  // ones are spread over every consumer warp of the grid and meet in the
+  // workspace behind one grid-wide counter.
+  const int nbat = (E + kRouterRowBatch - 1) / kRouterRowBatch;
+  float* lparts = reinterpret_cast<float*>(ring);  // [T][segment][E] when pl.localR
+  if (warp >= W) {
     const Tw* xg = static_cast<const Tw*>(a.x);
     const int nvec = H / VEC;  // the host guarantees H % VEC == 0 on this path
-    for (int idx = tid; idx < NT * nvec; idx += kThreads) {
+#pragma unroll 8
+    for (int idx = tid - W * 32; idx < NT * nvec; idx += kThreads - W * 32) {
       const int t = idx / nvec;
       const int v = idx - t * nvec;
       float f[VEC];
@@ -420,12 +404,58 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       for (int q = 0; q < VEC / 4; ++q)
         dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
     }
+  } else {
+    const Tw* gw = static_cast<const Tw*>(a.gate_w);
+    const Tw* xg = static_cast<const Tw*>(a.x);
+    const int items = T * nbat * kRouterSegments;
+    const int first = pl.localR ? warp : b + G * warp;
+    const int step = pl.localR ? W : G * W;
+    float* pbase = pl.localR ? lparts : a.rparts;
+    for (int it = first; it < items; it += step) {
+      const int seg = it % kRouterSegments;
+      const int rest = it / kRouterSegments;
+      const int eb = rest % nbat, t = rest / nbat;
+      const int e0 = eb * kRouterRowBatch;
+      router_segment_warp<Tw, XGlobal<Tw>>(
+          gw + (int64_t)e0 * H, XGlobal<Tw>{xg + (int64_t)t * H}, min(kRouterRowBatch, E - e0), H,
+          seg, lane, true, pbase + ((int64_t)t * kRouterSegments + seg) * E + e0);
+    }
   }
-
-  // ---- routing: logits come from k_router_logits (the grid we depend on) --
-  griddep_wait();
+  __syncthreads();
+  if (!pl.localR) {
+    if (tid == 0) {
+      // grid-wide: every CTA's partial sums are written
+      __threadfence();
+      red_release_gpu_add(&a.sync[kSyncRouter], 1u);
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_gpu(&a.sync[kSyncRouter]) < (uint32_t)G) {
+        if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // ---- logits (segment sums added in order, + bias) and top-K per token ----
+  for (int i = tid; i < T * E; i += kThreads) {
+    const int t = i / E, e = i - t * E;
+    float part[kRouterSegments];
+    const int64_t pt = (int64_t)t * kRouterSegments * E + e;
+#pragma unroll
+    for (int j = 0; j < kRouterSegments; ++j)  // workspace sums: read from L2 (other CTAs wrote them)
+      part[j] = pl.localR ? lparts[pt + j * E] : __ldcg(a.rparts + pt + j * E);
+    float l = part[0];
+#pragma unroll
+    for (int j = 1; j < kRouterSegments; ++j) l = __fadd_rn(l, part[j]);
+    if (a.bias) l = __fadd_rn(l, a.bias[e]);
+    s_logits[t * kMaxExperts + e] = l;
+  }
+  __syncthreads();
   if (warp < T)
-    select_topk_warp(a.logits + warp * E, E, K, lane, tok_ids + warp * kMaxExperts,
+    select_topk_warp(s_logits + warp * kMaxExperts, E, K, lane, tok_ids + warp * kMaxExperts,
                      tok_w + warp * kMaxExperts);
   __syncthreads();
   if (tid == 0) {
@@ -473,6 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   } else if (warp == W) {
     // =========================== producer ===================================
     if (lane == 0) {
+      // the ring held router partial sums (generic writes) until the selection
+      fence_proxy_async_smem();
       const uint64_t pol = l2_policy_evict_first();
       bool ok = true;
       int issued = 0;
@@ -795,6 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     const uint32_t prev = atomicAdd(&a.sync[kSyncExit], 1u);
     if (prev == (uint32_t)G - 1) {
       for (int s = 0; s < S; ++s) atomicExch(&a.sync[kSyncSlot0 + s], 0u);
+      atomicExch(&a.sync[kSyncRouter], 0u);
       atomicExch(&a.sync[kSyncExit], 0u);
       __threadfence();
     }
@@ -807,10 +840,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 enum LaunchMode { kModeUnknown = 0, kModeCoopPdl, kModePdl, kModeCoop };
 
 template <typename Tw, int NT>
-wr_status_t launch_pair(const FusedArgs& args, const void* x, const void* gate_w,
-                        const float* bias, float* logits, int grid, cudaStream_t stream) {
+wr_status_t launch_stream(const FusedArgs& args, int grid, cudaStream_t stream) {
   auto kern = k_fused_stream<Tw, NT>;
-  auto rkern = k_router_logits<Tw>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   static int mode[64];
@@ -819,22 +850,10 @@ wr_status_t launch_pair(const FusedArgs& args, const void* x, const void* gate_w
   std::call_once(once[dev & 63], [&] {
     attr_err[dev & 63] =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (attr_err[dev & 63] == cudaSuccess)
-      attr_err[dev & 63] = cudaFuncSetAttribute(
-          rkern, cudaFuncAttributeMaxDynamicSharedMemorySize, kVecMaxBytes);
   });
   if (attr_err[dev & 63] != cudaSuccess)
     return cuda_fail(attr_err[dev & 63], "cudaFuncSetAttribute(fused)");
 
-  // 1. router logits
-  const int H = args.H, E = args.E, T = args.T;
-  dim3 rgrid((E + 7) / 8, T);
-  rkern<<<rgrid, kConsumerThreads, (size_t)H * sizeof(float), stream>>>(
-      static_cast<const Tw*>(x), static_cast<const Tw*>(gate_w), bias, E, H, logits);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "k_router_logits launch");
-
-  // 2. the streaming kernel, dependent on (1)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -847,6 +866,7 @@ wr_status_t launch_pair(const FusedArgs& args, const void* x, const void* gate_w
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   int& m = mode[dev & 63];
   const int tries[3] = {kModeCoopPdl, kModePdl, kModeCoop};
+  cudaError_t e = cudaSuccess;
   for (int i = 0; i < 3; ++i) {
     const int mm = m != kModeUnknown ? m : tries[i];
     if (mm == kModeCoopPdl) { cfg.attrs = attr; cfg.numAttrs = 2; }
@@ -917,6 +937,15 @@ Plan make_plan(const Problem& p, int nt, int grid) {
   need += ((int64_t)kConsumerWarps * pl.NBM * nt * 4 + 63) / 64 * 64;
   const int64_t nst = need < kMiscOff ? (kMiscOff - need) / sb : 0;
   pl.nst = (int)(nst > kMaxStages ? kMaxStages : nst);
+  // Every CTA computes the whole router when it is small (<= 2 items per
+  // consumer warp, <= 64 KB of router weights read from L2 by each CTA, the
+  // partial sums fit in the ring); otherwise the items are spread over the grid.
+  const int64_t items =
+      (int64_t)nt * ((p.E + kRouterRowBatch - 1) / kRouterRowBatch) * kRouterSegments;
+  pl.localR = (items <= 2 * kConsumerWarps && (int64_t)p.E * p.H * elt <= 64 * 1024 &&
+               (int64_t)nt * kRouterSegments * p.E * 4 <= (int64_t)pl.nst * pl.SB)
+                  ? 1
+                  : 0;
   return pl;
 }
 
@@ -951,8 +980,9 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
   args.ids_out = ids;
   args.w_out = w;
   args.sync = static_cast<uint32_t*>(ws);
-  float* logits = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSyncBytes);
-  args.logits = logits;
+  args.gate_w = gate_w;
+  args.bias = p.router_bias;
+  args.rparts = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kSyncBytes);
   args.act = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kActOffset);
   args.E = p.E;
   args.H = p.H;
@@ -965,15 +995,14 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
   const int nt = nt_bucket(p.T);
   const int grid = device_sm_count();
   args.pl = make_plan(p, nt, grid);
-  const float* bias = p.router_bias;
   if (p.dtype == WR_DTYPE_BF16) {
-    if (nt == 1) return launch_pair<uint16_t, 1>(args, x, gate_w, bias, logits, grid, stream);
-    if (nt == 2) return launch_pair<uint16_t, 2>(args, x, gate_w, bias, logits, grid, stream);
-    return launch_pair<uint16_t, 4>(args, x, gate_w, bias, logits, grid, stream);
+    if (nt == 1) return launch_stream<uint16_t, 1>(args, grid, stream);
+    if (nt == 2) return launch_stream<uint16_t, 2>(args, grid, stream);
+    return launch_stream<uint16_t, 4>(args, grid, stream);
   }
-  if (nt == 1) return launch_pair<float, 1>(args, x, gate_w, bias, logits, grid, stream);
-  if (nt == 2) return launch_pair<float, 2>(args, x, gate_w, bias, logits, grid, stream);
-  return launch_pair<float, 4>(args, x, gate_w, bias, logits, grid, stream);
+  if (nt == 1) return launch_stream<float, 1>(args, grid, stream);
+  if (nt == 2) return launch_stream<float, 2>(args, grid, stream);
+  return launch_stream<float, 4>(args, grid, stream);
 }
 
 }  // namespace wr

@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(kRouterThreads) k_router(const Tw* __restrict_
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // blockDim.x == 32 * kRouterSegments: warp j computes segment j of every row.
-  router_segment_warp<Tw>(gate_w, xs, E, H, warp, lane, vec_ok, parts + warp * kMaxExperts);
+  router_segment_warp<Tw>(gate_w, XSmem{xs}, E, H, warp, lane, vec_ok, parts + warp * kMaxExperts);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     lg[e] = router_combine(parts, kMaxExperts, e, bias);

@@ -25,13 +25,34 @@ constexpr int kMaxExperts = 64;
 constexpr int kRouterSegments = 8;
 constexpr int kRouterRowBatch = 8;  // router rows a warp keeps in flight
 
-// Segment `seg` partial sums of rows [0, E) of gate_w against the fp32 vector
-// xs (shared memory), computed by one warp.  Writes part[e] (lane 0) for
-// every row.  vec_ok: rows and H allow 16-byte vector loads.
+// Where router_segment_warp reads x: an fp32 copy in shared memory, or the
+// caller's x in global memory (widened on the fly; widening is exact, so both
+// give the same fp32 values and the same sums).
+struct XSmem {
+  const float* p;
+  template <int VEC>
+  WR_DEVINL void vec(int v, float (&f)[VEC]) const {
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) f[q] = p[(int64_t)v * VEC + q];
+  }
+  WR_DEVINL float at(int j) const { return p[j]; }
+};
 template <typename Tw>
-WR_DEVINL void router_segment_warp(const Tw* __restrict__ gate_w, const float* __restrict__ xs,
-                                   int E, int H, int seg, int lane, bool vec_ok,
-                                   float* __restrict__ part) {
+struct XGlobal {
+  const Tw* p;
+  template <int VEC>
+  WR_DEVINL void vec(int v, float (&f)[VEC]) const {
+    Chunk<Tw>::widen(ldg_nc_v4(p + (int64_t)v * VEC), f);
+  }
+  WR_DEVINL float at(int j) const { return load_scalar<Tw>(p, j); }
+};
+
+// Segment `seg` partial sums of rows [0, E) of gate_w against x, computed by
+// one warp.  Writes part[e] (lane 0) for every row.  vec_ok: rows and H allow
+// 16-byte vector loads.
+template <typename Tw, typename XS = XSmem>
+WR_DEVINL void router_segment_warp(const Tw* __restrict__ gate_w, const XS xs, int E, int H,
+                                   int seg, int lane, bool vec_ok, float* __restrict__ part) {
   constexpr int VEC = Chunk<Tw>::kVec;
   constexpr int RB = kRouterRowBatch;
   const int nvec = (H + VEC - 1) / VEC;
@@ -47,10 +68,8 @@ WR_DEVINL void router_segment_warp(const Tw* __restrict__ gate_w, const float* _
 #pragma unroll
         for (int r = 0; r < RB; ++r)
           if (e0 + r < E) raw[r] = ldg_nc_v4(gate_w + (int64_t)(e0 + r) * H + (int64_t)v * VEC);
-        const float* xv = xs + (int64_t)v * VEC;
         float xf[VEC];
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) xf[q] = xv[q];
+        xs.template vec<VEC>(v, xf);
 #pragma unroll
         for (int r = 0; r < RB; ++r) {
           if (e0 + r < E) {
@@ -70,7 +89,7 @@ WR_DEVINL void router_segment_warp(const Tw* __restrict__ gate_w, const float* _
 #pragma unroll
           for (int q = 0; q < VEC; ++q) {
             const int j = v * VEC + q;
-            if (j < H) acc[r] = __fmaf_rn(load_scalar<Tw>(row, j), xs[j], acc[r]);
+            if (j < H) acc[r] = __fmaf_rn(load_scalar<Tw>(row, j), xs.at(j), acc[r]);
           }
         }
       }
