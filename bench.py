@@ -187,6 +187,10 @@ def cpu_composition_timing(x, gate_w, weight_buf, E, H, I, K, budget_s, max_call
 
 
 # ---------------------------------------------------------------------------
+def workload_name(args, world: int) -> str:
+    return f"{args.config}_bs1_{args.dtype}" + (f"_{args.parallel}{world}" if world > 1 else "")
+
+
 def run_reference_arm(args, world, rank):
     if rank != 0:
         return
@@ -206,8 +210,11 @@ def run_reference_arm(args, world, rank):
         "n_gpus": args.gpus, "steps": n, "warmup": 3, "ms_per_step": round(us / 1000, 4),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config}_bs1", "E": E, "H": H, "I": I, "top_k": K,
-                   "tokens": 1, "parallelism": "cpu"},
+        "config": {"workload": workload_name(args, world), "E": E, "H": H, "I": I, "top_k": K,
+                   "tokens": 1,
+                   "parallelism": f"{args.parallel}{world}" if world > 1 else "single",
+                   "reference_compute": "fp32 (warp-route's only dtype): the layer's "
+                                        f"{args.dtype} weights widened to fp32"},
         "cpu_baseline": {"value": round(us, 2), "unit": "us/layer", "cores": cores,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(us, 2), "unit": "us/layer", "h2d_bytes_per_step": 0,
@@ -274,8 +281,14 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
 
     # ---- device-resident timing ----
-    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps)]
-    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps)]
+    # One fused-kernel launch per step.  At N = 1 nothing else is on the
+    # stream, so the kernel's average launch duration is the timed region
+    # over the launches (launch gaps included); per-step events would sit
+    # between the kernels and stretch them.  At N > 1 an all-reduce follows
+    # every layer, so each layer call is bracketed by its own events.
+    per_step = world > 1
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -283,9 +296,11 @@ def run_ours(args, world, rank, local):
     with ClockSampler(local) as clk:
         t0.record(stream)
         for i in range(Ksteps):
-            k_start[i].record(stream)
+            if per_step:
+                k_start[i].record(stream)
             out = layer_call(layers[i % n_layers])
-            k_end[i].record(stream)
+            if per_step:
+                k_end[i].record(stream)
             if world > 1:
                 dist.all_reduce(out)
         t1.record(stream)
@@ -294,8 +309,11 @@ def run_ours(args, world, rank, local):
         dist.barrier()
     clocks = clk.summary()
     total_ms = t0.elapsed_time(t1)
-    kern_ms = [a.elapsed_time(b) for a, b in zip(k_start, k_end)]
-    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    if per_step:
+        kern_ms = [a.elapsed_time(b) for a, b in zip(k_start, k_end)]
+        kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    else:
+        kern_avg_ms = total_ms / Ksteps
     t = torch.tensor([total_ms, kern_avg_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -362,7 +380,7 @@ def run_ours(args, world, rank, local):
         peak, peak_kind = peaks()
         # the fused kernel's bytes per launch on the busiest rank (identical per rank for TP)
         achieved = avg_bytes / (kern_avg_ms * 1e-3) / 1e9
-        workload = f"{args.config}_bs1_{args.dtype}" + (f"_{args.parallel}{world}" if world > 1 else "")
+        workload = workload_name(args, world)
         traffic = ncu_traffic(workload)
         line = {
             "metric": METRIC, "value": round(us_per_layer, 3), "unit": "us/layer",
