@@ -55,6 +55,7 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "wr_common.cuh"
 #include "wr_internal.h"
@@ -181,6 +182,50 @@ WR_DEVINL void dot_pair(const uint4* __restrict__ gp, const uint4* __restrict__ 
         ua = fmaf(uf[4 * q4 + 2], x4.z, ua);
         ua = fmaf(uf[4 * q4 + 3], x4.w, ua);
       }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    g[t] += g1[t];
+    u[t] += u1[t];
+  }
+}
+
+// Two fp32 multiply-adds with bf16 inputs: acc += lo(w) * lo(x), then
+// acc += hi(w) * hi(x).  A bf16 product is exact in fp32 and each add rounds
+// once, so this equals fmaf on the widened values; the mixed-precision FMA
+// just needs no separate widening instruction.
+WR_DEVINL float fma2_bf16(uint32_t w, uint32_t x, float acc) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %1;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, wl, xl, %0;\n\t"
+      "fma.rn.f32.bf16 %0, wh, xh, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+  return acc;
+}
+
+// dot_pair for bf16 weights with x kept as bf16 chunks in shared memory
+// ([NT][H]); same elements, order and accumulators as dot_pair, so the same
+// fp32 results.
+template <int NT>
+WR_DEVINL void dot_pair_bf16(const uint4* __restrict__ gp, const uint4* __restrict__ up,
+                             const uint4* __restrict__ xs, int H, int c0, int j0, int j1,
+                             int lane, float (&g)[NT], float (&u)[NT]) {
+  float g1[NT], u1[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) g1[t] = u1[t] = 0.0f;
+#pragma unroll 4
+  for (int j = j0 + lane; j < j1; j += 32) {
+    const uint4 gw = gp[j], uw = up[j];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4 xv = xs[(t * H + c0) / 8 + j];
+      g[t] = fma2_bf16(gw.y, xv.y, fma2_bf16(gw.x, xv.x, g[t]));
+      u[t] = fma2_bf16(uw.y, xv.y, fma2_bf16(uw.x, xv.x, u[t]));
+      g1[t] = fma2_bf16(gw.w, xv.w, fma2_bf16(gw.z, xv.z, g1[t]));
+      u1[t] = fma2_bf16(uw.w, xv.w, fma2_bf16(uw.z, xv.z, u1[t]));
     }
   }
 #pragma unroll
@@ -330,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   constexpr int VEC = Chunk<Tw>::kVec;
   constexpr int ELT = (int)sizeof(Tw);
   constexpr int W = kConsumerWarps;
+  // bf16: x stays bf16 in shared memory and phase A uses mixed-precision FMAs
+  constexpr bool kBf16 = std::is_same<Tw, uint16_t>::value;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   const Plan pl = a.pl;
@@ -385,7 +432,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   // workspace behind one grid-wide counter.
   const int nbat = (E + kRouterRowBatch - 1) / kRouterRowBatch;
   float* lparts = reinterpret_cast<float*>(ring);  // [T][segment][E] when pl.localR
-  if (warp >= W) {
+  if (warp >= W && kBf16) {
+    // bf16 x kept as is: [NT][H] chunks (tokens >= T are zero)
+    const uint4* xg = static_cast<const uint4*>(a.x);
+    uint4* dst = reinterpret_cast<uint4*>(vreg);
+    const int nvec = H / VEC;
+#pragma unroll 8
+    for (int idx = tid - W * 32; idx < NT * nvec; idx += kThreads - W * 32)
+      dst[idx] = idx < T * nvec ? ldg_nc_v4(xg + idx) : make_uint4(0u, 0u, 0u, 0u);
+  } else if (warp >= W) {
     const Tw* xg = static_cast<const Tw*>(a.x);
     const int nvec = H / VEC;  // the host guarantees H % VEC == 0 on this path
 #pragma unroll 8
@@ -640,7 +695,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         if (pl.orderA != kOrderGlobal)
           for (; published < gr.s; ++published) publish(published);
         const int g = gr.g;
-        const int p0 = gr.s * I + gr.r;  // activation row of the group's first row pair
         const int first = (warp - (lrow & (W - 1)) + W) & (W - 1);  // my first row of the group
         const bool mine = first < g;
         lrow += g;
@@ -657,10 +711,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 #pragma unroll
                 for (int t = 0; t < NT; ++t) gg[k][t] = uv[k][t] = 0.0f;
                 const int rr = first + k * W;
-                if (rr < g)
-                  dot_pair<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.CWA * ELT),
-                                   reinterpret_cast<const uint4*>(st + (pl.GA + rr) * pl.CWA * ELT),
-                                   vreg, H, 0, 0, nch_full, lane, gg[k], uv[k]);
+                if (rr < g) {
+                  const uint4* gp = reinterpret_cast<const uint4*>(st + rr * pl.CWA * ELT);
+                  const uint4* up = reinterpret_cast<const uint4*>(st + (pl.GA + rr) * pl.CWA * ELT);
+                  if constexpr (kBf16)
+                    dot_pair_bf16<NT>(gp, up, reinterpret_cast<const uint4*>(vreg), H, 0, 0,
+                                      nch_full, lane, gg[k], uv[k]);
+                  else
+                    dot_pair<Tw, NT>(gp, up, vreg, H, 0, 0, nch_full, lane, gg[k], uv[k]);
+                }
               }
               __syncwarp();
               if (lane == 0) mbar_arrive(&empty[c.si]);
@@ -674,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
                   for (int t = 0; t < NT; ++t) {
                     if (lane == t) {
                       const float wt = slot_w[gr.s * NT + t];
-                      a.act[((int64_t)p0 + rr) * NT + t] =
+                      a.act[((int64_t)gr.s * I + gr.r + rr) * NT + t] =
                           (wt != 0.0f) ? wt * (silu(gg[k][t]) * uv[k][t]) : 0.0f;
                     }
                   }
@@ -682,9 +741,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
               }
             } else {
               // one row pair split over several stages (g == 1, first == 0)
-              dot_pair<Tw, NT>(reinterpret_cast<const uint4*>(st),
-                               reinterpret_cast<const uint4*>(st + pl.GA * pl.CWA * ELT), vreg, H,
-                               c0, 0, cw / VEC, lane, ga, ua);
+              if constexpr (kBf16)
+                dot_pair_bf16<NT>(reinterpret_cast<const uint4*>(st),
+                                  reinterpret_cast<const uint4*>(st + pl.GA * pl.CWA * ELT),
+                                  reinterpret_cast<const uint4*>(vreg), H, c0, 0, cw / VEC, lane,
+                                  ga, ua);
+              else
+                dot_pair<Tw, NT>(reinterpret_cast<const uint4*>(st),
+                                 reinterpret_cast<const uint4*>(st + pl.GA * pl.CWA * ELT), vreg, H,
+                                 c0, 0, cw / VEC, lane, ga, ua);
               __syncwarp();
               if (lane == 0) mbar_arrive(&empty[c.si]);
               if (c0 + cw >= H) {
@@ -694,7 +759,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
                 for (int t = 0; t < NT; ++t) {
                   if (lane == t) {
                     const float wt = slot_w[gr.s * NT + t];
-                    a.act[(int64_t)p0 * NT + t] = (wt != 0.0f) ? wt * (silu(ga[t]) * ua[t]) : 0.0f;
+                    a.act[((int64_t)gr.s * I + gr.r) * NT + t] =
+                        (wt != 0.0f) ? wt * (silu(ga[t]) * ua[t]) : 0.0f;
                   }
                 }
 #pragma unroll
