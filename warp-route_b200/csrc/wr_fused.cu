@@ -244,6 +244,32 @@ WR_DEVINL void dot_down(const uint4* __restrict__ wp, const float* __restrict__ 
   float acc1[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc1[t] = 0.0f;
+  if constexpr (VEC == 8 && NT == 1) {
+    // bf16, one token: a lane's 8 activations are 32 bytes, so lanes 4 apart
+    // would hit the same shared-memory banks.  Lanes with bit 2 set read the
+    // upper 16 bytes first (and take the weight halves in the same swapped
+    // order): each group of 8 lanes then covers 8 distinct bank slots.  Those
+    // lanes fill acc and acc1 in swapped roles, and acc + acc1 is the same.
+    const int hs = (j0 & 4) ? 4 : 0;
+#pragma unroll 4
+    for (int j = j0; j < nch; j += js) {
+      const uint4 w = wp[j];
+      const float4 aA = *reinterpret_cast<const float4*>(av + j * 8 + hs);
+      const float4 aB = *reinterpret_cast<const float4*>(av + j * 8 + (4 - hs));
+      const uint32_t wA0 = hs ? w.z : w.x, wA1 = hs ? w.w : w.y;
+      const uint32_t wB0 = hs ? w.x : w.z, wB1 = hs ? w.y : w.w;
+      acc[0] = fmaf(bf16lo(wA0), aA.x, acc[0]);
+      acc[0] = fmaf(bf16hi(wA0), aA.y, acc[0]);
+      acc[0] = fmaf(bf16lo(wA1), aA.z, acc[0]);
+      acc[0] = fmaf(bf16hi(wA1), aA.w, acc[0]);
+      acc1[0] = fmaf(bf16lo(wB0), aB.x, acc1[0]);
+      acc1[0] = fmaf(bf16hi(wB0), aB.y, acc1[0]);
+      acc1[0] = fmaf(bf16lo(wB1), aB.z, acc1[0]);
+      acc1[0] = fmaf(bf16hi(wB1), aB.w, acc1[0]);
+    }
+    acc[0] += acc1[0];
+    return;
+  }
 #pragma unroll 4
   for (int j = j0; j < nch; j += js) {
     float wf[VEC];
