@@ -146,7 +146,7 @@ WR_API wr_status_t wr_fused_moe(const wr_moe_desc_t* desc, const void* x,
  * device heap and gives the code it loads no workspace).  The scratch comes
  * from a 1 MiB array built into the library, which every GPU that loads the
  * library holds until the process exits; a layer that needs more (about
- * top_k * intermediate_dim * 4 + 1536 bytes) gets WR_ERR_UNSUPPORTED and
+ * top_k * intermediate_dim * 4 + 8704 bytes) gets WR_ERR_UNSUPPORTED and
  * nothing is launched.  All calls on one device share the array and its
  * control words are cleared on `stream` before each launch, so calls that
  * overlap on the GPU race: serialise them.  The first call on each device

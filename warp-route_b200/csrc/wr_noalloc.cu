@@ -4,8 +4,8 @@
 // Some hosts own the whole device heap — an inference server's memory pool,
 // a plugin interface that hands its plugins no workspace — and do not let
 // the code they load call cudaMalloc (which can also stall the device while
-// it runs).  wr_fused_moe needs a small device workspace (completion counters
-// and a status word, router logits, fp32 activations); this entry point takes it
+// it runs).  wr_fused_moe needs a small device workspace (counters and a status
+// word, router partial sums, fp32 activations); this entry point takes it
 // from a fixed array compiled into the library instead, so the caller passes
 // only inputs and outputs.
 //
@@ -13,7 +13,7 @@
 //   * every GPU that loads the library holds kNoAllocScratchBytes (1 MiB)
 //     of device memory until the process exits;
 //   * one decode token per call, and the layer's workspace must fit:
-//     roughly top_k * intermediate_dim * 4 + 1536 bytes <= 1 MiB (Mixtral,
+//     roughly top_k * intermediate_dim * 4 + 8704 bytes <= 1 MiB (Mixtral,
 //     DBRX and DeepSeek shapes fit); larger shapes are rejected with
 //     WR_ERR_UNSUPPORTED before anything is launched;
 //   * all calls on a device share the one array, which keeps the last call's
