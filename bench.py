@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="budget of the bounded CPU-baseline sample")
+    ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
+                    help="N > 1: sum the ranks' outputs inside the layer kernel over NVLink peer "
+                         "memory (fused) or with a separate NCCL all-reduce after it")
     ap.add_argument("--layers", type=int, default=0,
                     help="rotating layers (0: enough to exceed 4x L2 between reuses)")
     return ap.parse_args()
@@ -266,27 +269,39 @@ def run_ours(args, world, rank, local):
     bytes_per_layer = [synthetic.algorithmic_bytes(E, H, Il, u, 1, elt) for u in distinct]
     avg_bytes = sum(bytes_per_layer) / len(bytes_per_layer)
 
-    def layer_call(Lr):
+    # N > 1: every rank's partial output is summed inside the layer kernel
+    # (PeerComm, NVLink peer memory), or by a separate NCCL all-reduce.
+    fused_ar = world > 1 and args.allreduce == "fused"
+    comm = F.PeerComm(H) if fused_ar else None
+
+    def layer(Lr, x):
+        if fused_ar:
+            return F.fused_moe_allreduce(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K, comm,
+                                         ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)
         if ep > 1:
-            return F.fused_moe_routed(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
+            return F.fused_moe_routed(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
                                       ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)[0]
-        return F.fused_moe(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K)
+        return F.fused_moe(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K)
+
+    def reduce(out):
+        if world > 1 and not fused_ar:
+            dist.all_reduce(out)
 
     stream = torch.cuda.current_stream()
     W, Ksteps = args.warmup, args.steps
     for i in range(W):
-        out = layer_call(layers[i % n_layers])
-        if world > 1:
-            dist.all_reduce(out)
+        Lr = layers[i % n_layers]
+        reduce(layer(Lr, Lr.x))
     torch.cuda.synchronize()
 
     # ---- device-resident timing ----
-    # One fused-kernel launch per step.  At N = 1 nothing else is on the
-    # stream, so the kernel's average launch duration is the timed region
-    # over the launches (launch gaps included); per-step events would sit
-    # between the kernels and stretch them.  At N > 1 an all-reduce follows
-    # every layer, so each layer call is bracketed by its own events.
-    per_step = world > 1
+    # One fused-kernel launch per step (the all-reduce included when fused).
+    # When nothing else is on the stream, the kernel's average launch
+    # duration is the timed region over the launches (launch gaps included);
+    # per-step events would sit between the kernels and stretch them.  With
+    # a separate NCCL all-reduce, each layer call is bracketed by its own
+    # events.
+    per_step = world > 1 and not fused_ar
     k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -298,11 +313,11 @@ def run_ours(args, world, rank, local):
         for i in range(Ksteps):
             if per_step:
                 k_start[i].record(stream)
-            out = layer_call(layers[i % n_layers])
+            Lr = layers[i % n_layers]
+            out = layer(Lr, Lr.x)
             if per_step:
                 k_end[i].record(stream)
-            if world > 1:
-                dist.all_reduce(out)
+            reduce(out)
         t1.record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -330,10 +345,8 @@ def run_ours(args, world, rank, local):
     for i in range(min(W, 8)):
         Lr = layers[i % n_layers]
         x_dev[i % n_layers].copy_(x_host[i % n_layers], non_blocking=True)
-        o = F.fused_moe(x_dev[i % n_layers], Lr.gate_w, Lr.weight_buf, E, H, Il, K) if ep == 1 \
-            else layer_call(Lr)
-        if world > 1:
-            dist.all_reduce(o)
+        o = layer(Lr, x_dev[i % n_layers])
+        reduce(o)
         y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
     torch.cuda.synchronize()
     if world > 1:
@@ -344,13 +357,8 @@ def run_ours(args, world, rank, local):
         li = i % n_layers
         Lr = layers[li]
         x_dev[li].copy_(x_host[li], non_blocking=True)
-        if ep == 1:
-            o = F.fused_moe(x_dev[li], Lr.gate_w, Lr.weight_buf, E, H, Il, K)
-        else:
-            o = F.fused_moe_routed(x_dev[li], Lr.gate_w, Lr.weight_buf, E, H, Il, K,
-                                   ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)[0]
-        if world > 1:
-            dist.all_reduce(o)
+        o = layer(Lr, x_dev[li])
+        reduce(o)
         y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -389,6 +397,8 @@ def run_ours(args, world, rank, local):
             "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
             "config": {"workload": workload, "E": E, "H": H, "I": I, "top_k": K, "tokens": 1,
                        "parallelism": f"{args.parallel}{world}" if world > 1 else "single",
+                       "allreduce": (("fused in the layer kernel (NVLink peer memory)"
+                                      if fused_ar else "NCCL") if world > 1 else None),
                        "l2": f"inputs larger than L2: {n_layers} rotating layers, "
                              f"{avg_bytes / 1e6:.1f} MB streamed per step",
                        "layers_rotated": n_layers},
@@ -407,6 +417,10 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

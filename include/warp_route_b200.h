@@ -171,6 +171,45 @@ WR_API wr_status_t wr_batched_fused_moe(const wr_moe_desc_t* desc, int32_t num_t
                                  float* topk_weights, void* workspace,
                                  size_t workspace_bytes, wr_stream_t stream);
 
+/* ---- tensor- / expert-parallel layer with a fused all-reduce ---------- */
+
+/* Communicator of one rank for the all-reduce fused into the layer's last
+ * step (no warp-route counterpart: warp-route is single-GPU; it replaces the
+ * NCCL all-reduce a tensor- or expert-parallel caller would run after
+ * fused_moe_forward).  Ranks are the GPUs of one node, one process each.
+ * Set-up, once per process (allocates 512 * hidden_dim + 256 bytes of
+ * device memory on the current device):
+ *   wr_comm_create -> wr_comm_get_handle -> exchange the world_size handles
+ *   among the ranks (any host-side channel) -> wr_comm_open with all of them
+ *   in rank order.
+ * Every rank must then make the same sequence of wr_fused_moe_allreduce
+ * calls; a rank that stops makes the others' bounded waits give up
+ * (WR_ERR_TIMEOUT through wr_workspace_status) instead of hanging. */
+typedef struct wr_comm* wr_comm_t;
+
+/* Bytes of one rank's handle (a CUDA IPC memory handle). */
+WR_API size_t wr_comm_handle_bytes(void);
+WR_API wr_status_t wr_comm_create(int32_t rank, int32_t world_size, int32_t hidden_dim,
+                                  wr_comm_t* out);
+WR_API wr_status_t wr_comm_get_handle(wr_comm_t comm, void* handle);
+/* handles: world_size * wr_comm_handle_bytes() bytes, rank order. */
+WR_API wr_status_t wr_comm_open(wr_comm_t comm, const void* handles);
+WR_API wr_status_t wr_comm_destroy(wr_comm_t comm);
+
+/* num_tokens tokens through this rank's shard of the layer (a tensor-
+ * parallel slice of every expert's intermediate dimension, or an
+ * expert-parallel set of experts via desc->ep_*), with the ranks' partial
+ * outputs summed in rank order inside the same kernel: out [T,H] fp32 holds
+ * the full layer output, bit-identical on every rank.  Same arguments as
+ * wr_batched_fused_moe plus the communicator (desc->hidden_dim must equal
+ * the communicator's).  No warp-route counterpart (see wr_comm_t). */
+WR_API wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num_tokens,
+                                          const void* x, const void* gate_w,
+                                          const void* weight_buf, int64_t weight_buf_bytes,
+                                          float* out, int32_t* topk_ids, float* topk_weights,
+                                          void* workspace, size_t workspace_bytes,
+                                          wr_comm_t comm, wr_stream_t stream);
+
 /* ---- naive multi-kernel layer ----------------------------------------- */
 
 /* Scratch bytes for wr_naive_moe.  Replaces naive_moe_alloc_scratch /

@@ -116,8 +116,13 @@ size_t fused_ws_for(const Problem& p) {
   return fused > naive ? fused : naive;
 }
 
+// Blocks of up to 4 tokens through the streaming kernel (or the naive path
+// for shapes it does not take).  comm: all-reduce the ranks' partial outputs
+// inside each launch; the naive path has no all-reduce, so with a
+// communicator the shape must suit the streaming kernel.
 wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const void* wbuf,
-                      float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream) {
+                      float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream,
+                      const CommView* comm = nullptr) {
   if (p.T == 0) return WR_OK;
   const bool ptr_ok = aligned16(x) && aligned16(gate_w) && aligned16(wbuf);
   for (int t0 = 0; t0 < p.T; t0 += 4) {
@@ -130,7 +135,11 @@ wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const
     float* wq = w ? w + (size_t)t0 * p.K : nullptr;
     wr_status_t st;
     if (ptr_ok && aligned16(xq) && fused_supported(q))
-      st = launch_fused(q, xq, gate_w, wbuf, oq, iq, wq, ws, stream);
+      st = launch_fused(q, xq, gate_w, wbuf, oq, iq, wq, ws, stream, comm);
+    else if (comm)
+      st = fail(WR_ERR_UNSUPPORTED,
+                "the all-reduce layer needs the streaming kernel: 16-byte aligned x, gate_w and "
+                "weight_buf, and H, I multiples of 16 bytes of elements");
     else
       st = launch_naive(q, xq, gate_w, wbuf, oq, iq, wq, ws, stream);
     if (st != WR_OK) return st;
@@ -230,6 +239,27 @@ wr_status_t wr_batched_fused_moe(const wr_moe_desc_t* desc, int32_t num_tokens, 
   if ((st = check_ws(workspace, workspace_bytes, fused_ws_for(p))) != WR_OK) return st;
   return run_layer(p, x, gate_w, weight_buf, out, topk_ids, topk_weights, workspace,
                    static_cast<cudaStream_t>(stream));
+}
+
+wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num_tokens, const void* x,
+                                   const void* gate_w, const void* weight_buf,
+                                   int64_t weight_buf_bytes, float* out, int32_t* topk_ids,
+                                   float* topk_weights, void* workspace, size_t workspace_bytes,
+                                   wr_comm_t comm, wr_stream_t stream) {
+  Problem p;
+  wr_status_t st = make_problem(desc, num_tokens, &p);
+  if (st != WR_OK) return st;
+  if (!comm) return fail(WR_ERR_INVALID, "comm must not be NULL");
+  CommView v;
+  if ((st = comm_view(comm, &v)) != WR_OK) return st;
+  if (v.H != p.H)
+    return fail(WR_ERR_INVALID, "hidden_dim %d differs from the communicator's %d", p.H, v.H);
+  if (num_tokens == 0) return WR_OK;
+  if (!x || !gate_w || !out) return fail(WR_ERR_INVALID, "x, gate_w and out must not be NULL");
+  if ((st = check_weights(p, weight_buf, weight_buf_bytes)) != WR_OK) return st;
+  if ((st = check_ws(workspace, workspace_bytes, fused_ws_for(p))) != WR_OK) return st;
+  return run_layer(p, x, gate_w, weight_buf, out, topk_ids, topk_weights, workspace,
+                   static_cast<cudaStream_t>(stream), v.world > 1 ? &v : nullptr);
 }
 
 size_t wr_naive_moe_workspace_size(const wr_moe_desc_t* desc) {

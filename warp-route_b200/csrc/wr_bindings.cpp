@@ -123,7 +123,7 @@ void check_weight_buf(const torch::Tensor& hidden, const torch::Tensor& weight_b
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_impl(
     const torch::Tensor& hidden, const torch::Tensor& gate_w, const torch::Tensor& weight_buf,
     int E, int H, int I, int top_k, const c10::optional<torch::Tensor>& bias, int ep_first,
-    int ep_num, bool want_routing) {
+    int ep_num, bool want_routing, wr_comm_t comm = nullptr) {
   const bool one = hidden.dim() == 1;
   const int64_t T = one ? 1 : hidden.size(0);
   validate_2d(gate_w, "gate_w", E, H);
@@ -145,7 +145,13 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_impl(
   torch::Tensor ws = workspace_for(hidden.device(), stream, need);
   const int64_t wbytes = weight_buf.numel() * (int64_t)weight_buf.element_size();
   wr_status_t st;
-  if (one)
+  if (comm)
+    st = wr_fused_moe_allreduce(&d, (int32_t)T, hidden.data_ptr(), gate_w.data_ptr(),
+                                weight_buf.data_ptr(), wbytes, out.data_ptr<float>(),
+                                want_routing ? ids.data_ptr<int32_t>() : nullptr,
+                                want_routing ? w.data_ptr<float>() : nullptr, ws.data_ptr(),
+                                (size_t)ws.numel(), comm, stream);
+  else if (one)
     st = wr_fused_moe(&d, hidden.data_ptr(), gate_w.data_ptr(), weight_buf.data_ptr(), wbytes,
                       out.data_ptr<float>(), want_routing ? ids.data_ptr<int32_t>() : nullptr,
                       want_routing ? w.data_ptr<float>() : nullptr, ws.data_ptr(),
@@ -248,6 +254,49 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> router_topk(
   return {logits, ids, w};
 }
 
+// ---- communicator for the all-reduce fused into the layer ---------------
+// The handle is the C pointer as an integer; the Python wrapper owns it.
+
+int64_t comm_create(int rank, int world_size, int hidden_dim) {
+  wr_comm_t c = nullptr;
+  check_status(wr_comm_create(rank, world_size, hidden_dim, &c));
+  return reinterpret_cast<int64_t>(c);
+}
+
+torch::Tensor comm_handle(int64_t comm) {
+  torch::Tensor h = torch::empty({(int64_t)wr_comm_handle_bytes()}, torch::kUInt8);
+  check_status(wr_comm_get_handle(reinterpret_cast<wr_comm_t>(comm), h.data_ptr()));
+  return h;
+}
+
+void comm_open(int64_t comm, torch::Tensor handles) {
+  TORCH_CHECK(handles.device().is_cpu() && handles.scalar_type() == torch::kUInt8 &&
+                  handles.is_contiguous(),
+              "handles must be a contiguous uint8 CPU tensor");
+  check_status(wr_comm_open(reinterpret_cast<wr_comm_t>(comm), handles.data_ptr()));
+}
+
+void comm_destroy(int64_t comm) { check_status(wr_comm_destroy(reinterpret_cast<wr_comm_t>(comm))); }
+
+// This rank's shard of the layer with the ranks' outputs summed in-kernel:
+// (out fp32 [..,H], ids int32 [T,K], weights fp32 [T,K]).
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_moe_allreduce(
+    torch::Tensor hidden, torch::Tensor gate_w, torch::Tensor weight_buf, int num_experts,
+    int hidden_dim, int intermediate_dim, int top_k, int64_t comm,
+    c10::optional<torch::Tensor> router_bias, int ep_first_expert, int ep_num_local) {
+  CHECK_CUDA(hidden);
+  CHECK_CONTIGUOUS(hidden);
+  CHECK_DTYPE(hidden);
+  TORCH_CHECK(comm != 0, "comm must not be NULL");
+  TORCH_CHECK((hidden.dim() == 1 && hidden.size(0) == hidden_dim) ||
+                  (hidden.dim() == 2 && hidden.size(1) == hidden_dim),
+              "hidden must have shape [", hidden_dim, "] or [batch_size, ", hidden_dim,
+              "], got shape ", hidden.sizes());
+  return fused_impl(hidden, gate_w, weight_buf, num_experts, hidden_dim, intermediate_dim, top_k,
+                    router_bias, ep_first_expert, ep_num_local, true,
+                    reinterpret_cast<wr_comm_t>(comm));
+}
+
 int64_t workspace_status(torch::Tensor hidden) {
   // Reads and clears the status word of this device/stream's cached workspace.
   const c10::cuda::CUDAGuard guard(hidden.device());
@@ -273,6 +322,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &router_topk, "Router + softmax + top-K: (logits, ids, weights)",
         py::arg("hidden"), py::arg("gate_w"), py::arg("num_experts"), py::arg("hidden_dim"),
         py::arg("top_k"), py::arg("router_bias") = py::none());
+  m.def("comm_create", &comm_create, "Communicator of one rank (returns an opaque handle)",
+        py::arg("rank"), py::arg("world_size"), py::arg("hidden_dim"));
+  m.def("comm_handle", &comm_handle, "This rank's IPC handle bytes (uint8 CPU tensor)");
+  m.def("comm_open", &comm_open, "Map every rank's buffer (handles in rank order)");
+  m.def("comm_destroy", &comm_destroy, "Unmap and free a communicator");
+  m.def("fused_moe_allreduce", &fused_moe_allreduce,
+        "This rank's shard of the layer with the ranks' outputs summed in the same kernel",
+        py::arg("hidden"), py::arg("gate_w"), py::arg("weight_buf"), py::arg("num_experts"),
+        py::arg("hidden_dim"), py::arg("intermediate_dim"), py::arg("top_k"), py::arg("comm"),
+        py::arg("router_bias") = py::none(), py::arg("ep_first_expert") = 0,
+        py::arg("ep_num_local") = 0);
   m.def("workspace_status", &workspace_status,
         "Read and clear the device status word of the current stream's workspace");
   m.def("version", []() { return std::string(wr_version()); });

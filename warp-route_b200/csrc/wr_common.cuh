@@ -40,6 +40,7 @@ enum : uint32_t {
   DEV_TIMEOUT_GRID = 1u << 2,   // grid-wide barrier gave up
   DEV_TIMEOUT_ACT = 1u << 3,    // activation-window copy never landed
   DEV_TIMEOUT_DRAIN = 1u << 4,  // copies still in flight at exit
+  DEV_TIMEOUT_PEER = 1u << 5,   // a peer rank's partial outputs never arrived
 };
 
 // Wall-clock bound of every spin in these kernels (ns).  A healthy wait is
@@ -149,15 +150,15 @@ WR_DEVINL uint32_t ld_acquire_gpu(const uint32_t* p) {
 WR_DEVINL void red_release_gpu_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// The same at CTA scope on a shared-memory word.
-WR_DEVINL uint32_t ld_acquire_cta_smem(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+// System scope (other GPUs of the node read or write the word), relaxed:
+// single-copy atomic for aligned 64-bit words.
+WR_DEVINL uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-WR_DEVINL void red_release_cta_smem_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v)
-               : "memory");
+WR_DEVINL void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // 16-byte read-only global load that does not allocate in L1.

@@ -85,6 +85,7 @@ constexpr int kOffBars = 0;        // full[12], empty[12], act
 constexpr int kOffAbort = 256;     // int
 constexpr int kOffNSlots = 260;    // int
 constexpr int kOffSlotTag = 264;   // int [12]: stage number each ring slot currently holds
+constexpr int kOffEpoch = 320;     // uint32: this launch's all-reduce epoch
 constexpr int kOffSlotE = 512;     // int [64]: local expert of each slot
 constexpr int kOffSlotW = 768;     // float [64 * NT]: routing weight (0: not routed)
 constexpr int kOffTokIds = 1792;   // int [NT * 64]
@@ -141,6 +142,7 @@ struct FusedArgs {
   int ep_first, ep_num;
   Layout lay;
   Plan pl;
+  CommView comm;  // comm.world == 1: no all-reduce
 };
 
 WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts; }
@@ -447,6 +449,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   // kernel may begin its launch now: its CTAs take over SMs as ours exit.
   griddep_wait();
   griddep_launch_dependents();
+  uint32_t* s_epoch = reinterpret_cast<uint32_t*>(misc + kOffEpoch);
+  if (tid == 0 && a.comm.world > 1) *s_epoch = *a.comm.epoch + 1;  // read after the previous launch
+  // Output value v of token t, row h: into `out`, or with an all-reduce as
+  // the word (v | epoch << 32) into this rank's slot of every rank's
+  // mailbox (*s_epoch is read after the __syncthreads below, before use).
+  auto emit = [&](int t, int h, float v) {
+    if (a.comm.world > 1) {
+      const uint32_t e = *s_epoch;
+      const uint64_t word = ((uint64_t)e << 32) | __float_as_uint(v);
+      const size_t off =
+          (((size_t)a.comm.rank * 2 + (e & 1u)) * kCommMaxTokens + t) * (size_t)H + h;
+      for (int q = 0; q < a.comm.world; ++q) st_relaxed_sys_u64(a.comm.box[q] + off, word);
+    } else {
+      a.out[(int64_t)t * H + h] = v;
+    }
+  };
 
   // ---- x -> shared memory as fp32 [NT][H] (tokens >= T are zero), by the
   // producer and publisher warps, while the consumer warps compute the router
@@ -579,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     // No local expert selected (expert-parallel rank): this rank adds zero.
     for (int idx = tid; idx < T * nb; idx += kThreads) {
       const int t = idx / nb;
-      a.out[(int64_t)t * H + hb0 + (idx - t * nb)] = 0.0f;
+      emit(t, hb0 + (idx - t * nb), 0.0f);
     }
   } else if (warp == W) {
     // =========================== producer ===================================
@@ -892,14 +910,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         }
       }
       named_bar_sync(kBarConsumers, kConsumerThreads);  // all row accumulators final
-      if (ok && !*abort_flag) {
+      // (with an all-reduce the rows are written even after a failed wait,
+      // so the peers' waits end; the status word reports the failure)
+      if ((ok && !*abort_flag) || a.comm.world > 1) {
         for (int idx = tid; idx < T * nb; idx += kConsumerThreads) {
           const int t = idx / nb;
           const int h = idx - t * nb;
           float o = rowacc[h * NT + t];
 #pragma unroll
           for (int w = 1; w < W; ++w) o += rowacc[((int64_t)w * pl.NBM + h) * NT + t];
-          a.out[(int64_t)t * H + hb0 + h] = o;
+          emit(t, hb0 + h, o);
         }
       }
       if (tid == 0 && act_issued > 0 && !ok) {
@@ -912,6 +932,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   }
 
   __syncthreads();
+  if (a.comm.world > 1) {
+    // ---- one-shot all-reduce: this CTA's rows of every rank ----
+    // Each word of this rank's mailbox is polled until it carries this
+    // launch's epoch; the values are summed in source-rank order.
+    const uint32_t e = *s_epoch;
+    const uint64_t t0 = globaltimer_ns();
+    bool late = false;
+    for (int idx = tid; idx < T * nb; idx += kThreads) {
+      const int t = idx / nb;
+      const int h = hb0 + (idx - t * nb);
+      float o = 0.0f;
+      for (int q = 0; q < a.comm.world; ++q) {
+        const uint64_t* p =
+            a.comm.box[a.comm.rank] + (((size_t)q * 2 + (e & 1u)) * kCommMaxTokens + t) * H + h;
+        uint64_t w = ld_relaxed_sys_u64(p);
+        for (uint32_t spin = 1; (uint32_t)(w >> 32) != e && !late; ++spin) {
+          if ((spin & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_PEER);
+            late = true;
+          }
+          w = ld_relaxed_sys_u64(p);
+        }
+        o += __uint_as_float((uint32_t)w);
+      }
+      a.out[(int64_t)t * H + h] = o;
+    }
+  }
   if (tid == 0) {
     // Self-reset of the slot counters: every CTA has left its waits once it
     // counts itself out, so the last one can clear them all.
@@ -920,6 +967,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     if (prev == (uint32_t)G - 1) {
       for (int s = 0; s < S; ++s) atomicExch(&a.sync[kSyncSlot0 + s], 0u);
       atomicExch(&a.sync[kSyncRouter], 0u);
+      if (a.comm.world > 1) *a.comm.epoch = *s_epoch;  // the next launch uses epoch + 1
       atomicExch(&a.sync[kSyncExit], 0u);
       __threadfence();
     }
@@ -1064,8 +1112,15 @@ size_t fused_workspace_bytes(const Problem& p) {
 }
 
 wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, const void* wbuf,
-                         float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream) {
+                         float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream,
+                         const CommView* comm) {
   FusedArgs args;
+  if (comm) {
+    args.comm = *comm;
+  } else {
+    args.comm = CommView{};
+    args.comm.world = 1;
+  }
   args.x = x;
   args.wbuf = static_cast<const uint8_t*>(wbuf);
   args.out = out;

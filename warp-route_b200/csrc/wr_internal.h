@@ -15,6 +15,24 @@ namespace wr {
 // its scratch behind them so both can share one workspace.
 constexpr size_t kWsControlBytes = 512;
 
+// ---- peer-memory all-reduce (wr_comm.cu) ----
+constexpr int kMaxRanks = 8;
+constexpr int kCommMaxTokens = 4;   // tokens of one kernel launch
+
+// What the fused kernel needs of a communicator: every rank's mailbox,
+// mapped into this process, and this rank's launch counter.  A mailbox is
+// [source rank][2 parities][kCommMaxTokens][H] 64-bit words, each the fp32
+// partial output of one (token, row) in its low half and the epoch of the
+// launch that wrote it in its high half.
+struct CommView {
+  uint64_t* box[kMaxRanks];
+  uint32_t* epoch;
+  int rank, world, H;
+};
+
+// The kernel's view of an open communicator on the current device.
+wr_status_t comm_view(const wr_comm* c, CommView* v);
+
 // Per-call problem description after validation.
 struct Problem {
   int E, H, I, K, T;          // experts, hidden, intermediate, top_k, tokens
@@ -34,9 +52,11 @@ wr_status_t cuda_fail(cudaError_t e, const char* what);
 // True when the streaming kernel can take this problem (alignment, sizes).
 bool fused_supported(const Problem& p);
 size_t fused_workspace_bytes(const Problem& p);
+// comm: null, or the communicator whose ranks' partial outputs are summed
+// into `out` (identical on every rank).
 wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
                          const void* wbuf, float* out, int32_t* ids, float* w,
-                         void* ws, cudaStream_t stream);
+                         void* ws, cudaStream_t stream, const CommView* comm = nullptr);
 
 // ---- router kernel (wr_naive.cu) ----
 wr_status_t launch_router(const Problem& p, const void* x, const void* gate_w,

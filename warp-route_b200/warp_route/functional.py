@@ -174,3 +174,79 @@ def router_topk(
     """Router only: (logits fp32 [T,E], ids int32 [T,K], weights fp32 [T,K])."""
     _C = _load_extension()
     return _C.router_topk(x, gate_w, num_experts, hidden_dim, top_k, router_bias)
+
+
+def exchange_handles(mine: bytes, group=None) -> bytes:
+    """Every rank's handle bytes, concatenated in rank order (collective over
+    `group`; every handle must have the same length)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    handles: List[Optional[bytes]] = [None] * world
+    dist.all_gather_object(handles, mine, group=group)
+    if any(h is None or len(h) != len(mine) for h in handles):
+        raise RuntimeError("communicator handles of different sizes")
+    return b"".join(handles)
+
+
+class PeerComm:
+    """One rank's communicator for the all-reduce fused into the layer.
+
+    Tensor- or expert-parallel layers on the GPUs of one node, one process
+    per GPU: each rank streams its shard of the weights and the ranks'
+    partial outputs are summed (rank order, identical on every rank) in the
+    same kernel, over NVLink peer memory, instead of a separate NCCL
+    all-reduce.  Construction is collective over `group` (the ranks exchange
+    CUDA IPC handles through torch.distributed); every rank must then make
+    the same sequence of `fused_moe_allreduce` calls.  No warp-route
+    counterpart (warp-route is single-GPU).
+    """
+
+    def __init__(self, hidden_dim: int, group=None):
+        import torch.distributed as dist
+
+        _C = _load_extension()
+        self.rank = dist.get_rank(group)
+        self.world_size = dist.get_world_size(group)
+        self.hidden_dim = hidden_dim
+        self._ptr = _C.comm_create(self.rank, self.world_size, hidden_dim)
+        all_handles = exchange_handles(bytes(_C.comm_handle(self._ptr).numpy()), group)
+        _C.comm_open(self._ptr, torch.frombuffer(bytearray(all_handles), dtype=torch.uint8))
+
+    @property
+    def handle(self) -> int:
+        if self._ptr == 0:
+            raise RuntimeError("communicator is closed")
+        return self._ptr
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (call on every
+        rank, after the last layer call has finished)."""
+        if self._ptr:
+            _load_extension().comm_destroy(self._ptr)
+            self._ptr = 0
+
+
+def fused_moe_allreduce(
+    x: torch.Tensor,
+    gate_w: torch.Tensor,
+    weight_buf: torch.Tensor,
+    num_experts: int,
+    hidden_dim: int,
+    intermediate_dim: int,
+    top_k: int,
+    comm: PeerComm,
+    *,
+    router_bias: Optional[torch.Tensor] = None,
+    ep_first_expert: int = 0,
+    ep_num_local: int = 0,
+) -> torch.Tensor:
+    """This rank's shard of the layer with every rank's output summed in the
+    same kernel: x [H] or [T,H] -> float32, the full layer output on every
+    rank.  weight_buf holds this rank's shard: a tensor-parallel slice
+    (intermediate_dim = this rank's columns) or, with ep_num_local > 0, the
+    experts [ep_first_expert, ep_first_expert + ep_num_local)."""
+    _C = _load_extension()
+    return _C.fused_moe_allreduce(x, gate_w, weight_buf, num_experts, hidden_dim,
+                                  intermediate_dim, top_k, comm.handle, router_bias,
+                                  ep_first_expert, ep_num_local)[0]
