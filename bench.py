@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
                     help="N > 1: sum the ranks' outputs inside the layer kernel over NVLink peer "
                          "memory (fused) or with a separate NCCL all-reduce after it")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time the layer calls eagerly instead of replaying a CUDA graph of them")
     ap.add_argument("--layers", type=int, default=0,
                     help="rotating layers (0: enough to exceed 4x L2 between reuses)")
     return ap.parse_args()
@@ -302,6 +304,34 @@ def run_ours(args, world, rank, local):
     # a separate NCCL all-reduce, each layer call is bracketed by its own
     # events.
     per_step = world > 1 and not fused_ar
+    # Serving replays decode steps from CUDA graphs: the timed steps are
+    # replays of a graph of the rotating layers' calls (exactly K calls;
+    # capture and warm-up happen before the timed region).  The NCCL
+    # all-reduce comparison runs eagerly.
+    use_graph = not args.no_graph and not per_step
+    graphs = []
+    if use_graph:
+        cap_stream = torch.cuda.Stream()
+        with torch.cuda.stream(cap_stream):  # warm up on the capture stream (its workspace)
+            for _ in range(2):
+                for Lr in layers:
+                    layer(Lr, Lr.x)
+        torch.cuda.synchronize()
+
+        def capture(n):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap_stream):
+                for i in range(n):
+                    Lr = layers[i % n_layers]
+                    layer(Lr, Lr.x)
+            return g
+
+        g_full = capture(n_layers)
+        rem = Ksteps % n_layers
+        graphs = [g_full] * (Ksteps // n_layers) + ([capture(rem)] if rem else [])
+        for _ in range(2):
+            g_full.replay()
+        torch.cuda.synchronize()
     k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -310,14 +340,18 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         t0.record(stream)
-        for i in range(Ksteps):
-            if per_step:
-                k_start[i].record(stream)
-            Lr = layers[i % n_layers]
-            out = layer(Lr, Lr.x)
-            if per_step:
-                k_end[i].record(stream)
-            reduce(out)
+        if use_graph:
+            for g in graphs:
+                g.replay()
+        else:
+            for i in range(Ksteps):
+                if per_step:
+                    k_start[i].record(stream)
+                Lr = layers[i % n_layers]
+                out = layer(Lr, Lr.x)
+                if per_step:
+                    k_end[i].record(stream)
+                reduce(out)
         t1.record(stream)
         torch.cuda.synchronize()
     if world > 1:
@@ -368,6 +402,9 @@ def run_ours(args, world, rank, local):
     e2e_us = te.item() * 1000.0 / Ke
     # A bounded device wait that gave up would make the timings meaningless.
     status = F._load_extension().workspace_status(layers[0].x)
+    if use_graph:
+        with torch.cuda.stream(cap_stream):  # the workspace the graph's launches used
+            status = status or F._load_extension().workspace_status(layers[0].x)
     if status != 0:
         raise SystemExit(f"fused kernel reported device status {status}: timing discarded")
 
@@ -401,7 +438,9 @@ def run_ours(args, world, rank, local):
                                       if fused_ar else "NCCL") if world > 1 else None),
                        "l2": f"inputs larger than L2: {n_layers} rotating layers, "
                              f"{avg_bytes / 1e6:.1f} MB streamed per step",
-                       "layers_rotated": n_layers},
+                       "layers_rotated": n_layers,
+                       "timing": ("CUDA-graph replay of the layer calls" if use_graph
+                                  else "eager layer calls")},
             "hbm_gbs": round(avg_bytes / (us_per_layer * 1e-6) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
