@@ -11,9 +11,11 @@ tensor-parallel over N GPUs.  Inputs are synthetic and seeded; layers rotate
 so every step streams weights from HBM (each step reads more than L2 holds).
 
 Rank 0 prints one JSON line.  `value` is µs per layer (max over ranks, CUDA
-events on the launching stream); `e2e` is the same through the public API
-with the token copied in from pinned host memory and the output copied back
-every step; `roofline` relates the fused kernel's algorithmic bytes to the
+events on the launching stream; the timed steps replay a CUDA graph of the
+layer calls); `e2e` is the same through the public API, eagerly, with the
+token copied in from pinned host memory and the output copied back every step
+(copies on their own streams, overlapping the kernels); `roofline` relates
+the fused kernel's algorithmic bytes to the
 measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
 composition (restated in oracle/torch_composition.py) on a bounded sample.
 `--impl reference` times that CPU composition alone, as the reference arm.
@@ -370,30 +372,49 @@ def run_ours(args, world, rank, local):
     us_per_layer = total_ms * 1000.0 / Ksteps
 
     # ---- end-to-end through the public API, host buffers in and out ----
+    # Every step copies its token in from pinned host memory and its output
+    # back to pinned host memory.  The copies run on their own streams, as a
+    # serving loop would run them: step i+1's input copy and step i's output
+    # read overlap the layer kernels; events keep each step's copy-in before
+    # its layer and its copy-out after it.  The timed region ends when the
+    # last output has reached the host.
     Ke = Ksteps
     x_host = [torch.empty(H, dtype=dt).pin_memory() for _ in range(n_layers)]
     for li, Lr in enumerate(layers):
         x_host[li].copy_(Lr.x.cpu())
     y_host = torch.empty(Ke if Ke <= 4096 else 4096, H, dtype=torch.float32).pin_memory()
-    x_dev = [torch.empty(H, dtype=dt, device=dev) for _ in range(n_layers)]
-    for i in range(min(W, 8)):
-        Lr = layers[i % n_layers]
-        x_dev[i % n_layers].copy_(x_host[i % n_layers], non_blocking=True)
-        o = layer(Lr, x_dev[i % n_layers])
+    NB = 2  # device input buffers in flight
+    x_dev = [torch.empty(H, dtype=dt, device=dev) for _ in range(NB)]
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(NB)]
+    ev_read = [torch.cuda.Event() for _ in range(NB)]  # the layer that read x_dev[b] is done
+
+    def e2e_step(i):
+        b, li = i % NB, i % n_layers
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(ev_read[b])
+            x_dev[b].copy_(x_host[li], non_blocking=True)
+            ev_in[b].record(h2d)
+        stream.wait_event(ev_in[b])
+        o = layer(layers[li], x_dev[b])
         reduce(o)
-        y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+        ev_read[b].record(stream)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev_read[b])
+            o.record_stream(d2h)
+            y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+
+    for i in range(min(W, 8)):
+        e2e_step(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    h2d.wait_event(e0)
     for i in range(Ke):
-        li = i % n_layers
-        Lr = layers[li]
-        x_dev[li].copy_(x_host[li], non_blocking=True)
-        o = layer(Lr, x_dev[li])
-        reduce(o)
-        y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+        e2e_step(i)
+    stream.wait_stream(d2h)
     e1.record(stream)
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], device=dev)
