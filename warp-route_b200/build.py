@@ -31,7 +31,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
                      "-I" + INCLUDE, "-I" + CSRC]
-KERNEL_SOURCES = ["wr_api.cu", "wr_fused.cu", "wr_naive.cu", "wr_noalloc.cu", "wr_comm.cu"]
+KERNEL_SOURCES = ["wr_api.cu", "wr_fused.cu", "wr_naive.cu", "wr_noalloc.cu", "wr_comm.cu",
+                  "wr_grouped.cu"]
 HEADERS = ["wr_common.cuh", "wr_router.cuh", "wr_internal.h"]
 
 

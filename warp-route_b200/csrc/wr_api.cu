@@ -106,14 +106,21 @@ wr_status_t check_ws(void* ws, size_t have, size_t need) {
 }
 
 size_t fused_ws_for(const Problem& p) {
-  // The batched entry point runs blocks of up to 4 tokens through the
-  // streaming kernel; unsupported shapes go through the naive path.
+  // Batches of kGroupedMinTokens or more bf16 tokens run as grouped GEMMs;
+  // otherwise the batched entry point runs blocks of up to 4 tokens through
+  // the streaming kernel, and unsupported shapes go through the naive path.
   Problem q = p;
   q.T = p.T < 1 ? 1 : (p.T > 4 ? 4 : p.T);
-  const size_t naive = naive_workspace_bytes(p);
-  if (!fused_supported(q)) return naive;
-  const size_t fused = fused_workspace_bytes(q);
-  return fused > naive ? fused : naive;
+  size_t need = naive_workspace_bytes(p);
+  if (fused_supported(q)) {
+    const size_t fused = fused_workspace_bytes(q);
+    need = fused > need ? fused : need;
+  }
+  if (grouped_supported(p)) {
+    const size_t g = grouped_workspace_bytes(p);
+    need = g > need ? g : need;
+  }
+  return need;
 }
 
 // Blocks of up to 4 tokens through the streaming kernel (or the naive path
@@ -125,6 +132,8 @@ wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const
                       const CommView* comm = nullptr) {
   if (p.T == 0) return WR_OK;
   const bool ptr_ok = aligned16(x) && aligned16(gate_w) && aligned16(wbuf);
+  if (!comm && ptr_ok && grouped_supported(p))
+    return launch_grouped(p, x, gate_w, wbuf, out, ids, w, ws, stream);
   for (int t0 = 0; t0 < p.T; t0 += 4) {
     Problem q = p;
     q.T = p.T - t0 < 4 ? p.T - t0 : 4;

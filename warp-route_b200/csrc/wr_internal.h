@@ -58,6 +58,16 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
                          const void* wbuf, float* out, int32_t* ids, float* w,
                          void* ws, cudaStream_t stream, const CommView* comm = nullptr);
 
+// ---- grouped tensor-core path for token batches (wr_grouped.cu) ----
+// Batches of at least this many tokens run as grouped GEMMs over tokens
+// bucketed per expert.
+constexpr int kGroupedMinTokens = 16;
+bool grouped_supported(const Problem& p);
+size_t grouped_workspace_bytes(const Problem& p);
+wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w,
+                           const void* wbuf, float* out, int32_t* ids, float* w, void* ws,
+                           cudaStream_t stream);
+
 // ---- router kernel (wr_naive.cu) ----
 wr_status_t launch_router(const Problem& p, const void* x, const void* gate_w,
                           float* logits, int32_t* ids, float* w, cudaStream_t stream);
