@@ -211,4 +211,13 @@ WR_DEVINL float load_scalar<float>(const float* p, int64_t i) {
 
 WR_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// Programmatic dependent launch: wait for the previous kernel on the stream
+// (complete, memory visible) / let the next one be scheduled.  Both are
+// no-ops for a kernel launched without the programmatic-serialization
+// attribute.
+WR_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+WR_DEVINL void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace wr

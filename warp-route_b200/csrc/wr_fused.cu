@@ -147,11 +147,6 @@ struct FusedArgs {
 
 WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts; }
 
-WR_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-WR_DEVINL void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // Phase A dot products of one gate row and one up row over chunks [j0, j1)
 // (16-byte chunks of VEC elements starting at column c0) against x.
 template <typename Tw, int NT>

@@ -18,23 +18,27 @@
 //                   accumulators in TMEM over K = H, epilogue
 //                   act = silu(g) * u * w(token, k) stored as bf16 hi + lo
 //   k_grouped_gemm<down>
-//                   per (expert, 128 rows of H, K split, <=128 tokens):
-//                   Wd . act_hi + Wd . act_lo (the hi/lo pair keeps the
-//                   activation to ~16 mantissa bits), fp32 partials per split
-//   k_combine       out[t] = sum over k (ascending) and splits (ascending):
-//                   one fixed order, so the result is deterministic.
+//                   per (expert, 128 rows of H, <=128 tokens): Wd . act_hi +
+//                   Wd . act_lo (the hi/lo pair keeps the activation to ~16
+//                   mantissa bits); the K chunks of all tiles are dealt to
+//                   the CTAs in equal ranges (stream-K), a tile cut by a
+//                   range boundary leaves one fp32 partial per CTA
+//   k_combine       out[t] = sum over k (ascending) of the partials of its
+//                   row (in CTA order): one fixed order, so the result is
+//                   deterministic.
 //
 // GEMM structure: weights are the MMA's A operand (M = 128 weight rows,
 // K-major: rows of the packed layout are contiguous along K), tokens the B
 // operand (N = 16..128, K-major), both bf16, accumulator fp32 in TMEM.  One
-// persistent CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected
-// lane, 128-byte swizzled tiles), warp 1 owns TMEM and issues the MMAs (one
-// elected lane, tcgen05.commit to release smem stages and to hand
-// accumulators to the epilogue), warps 2-5 read the accumulators back with
-// tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31) and store the results.
-// Two accumulator buffers let the epilogue of one tile overlap the MMAs of
-// the next.  No TMA multicast anywhere; every wait is bounded and a wait
-// that runs out sets the workspace status word and winds the CTA down
+// persistent CTA per SM, 7 warps: warp 0 issues the weight TMA loads into a
+// deep ring (they come from HBM), warp 6 the token-tile loads into a shallow
+// ring (they come from L2), both 128-byte swizzled; warp 1 owns TMEM and
+// issues the MMAs (one elected lane, tcgen05.commit to release smem stages
+// and to hand accumulators to the epilogue); warps 2-5 read the accumulators
+// back with tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31) and store the
+// results.  Two accumulator buffers let the epilogue of one tile overlap the
+// MMAs of the next.  No TMA multicast anywhere; every wait is bounded and a
+// wait that runs out sets the workspace status word and winds the CTA down
 // (copies in flight drained, MMAs completed, TMEM freed).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -49,29 +53,40 @@
 namespace wr {
 namespace {
 
-constexpr int kBM = 128;                  // weight rows per tile (MMA M)
-constexpr int kBK = 64;                   // K elements per smem stage: one 128-byte swizzle row
-constexpr int kNMax = 128;                // tokens per tile (MMA N)
-constexpr int kTileA = kBM * kBK * 2;     // 16 KB of weights per operand per stage
-constexpr int kRowB = kBK * 2;            // bytes of one token row per stage
-constexpr int kBoxRows = 16;              // token rows per TMA box
-constexpr int kGemmThreads = 192;
-constexpr int kTmemCols = 512;            // two accumulator buffers of 256 columns
-constexpr int kAccStride = 256;           // columns between accumulator buffers
-constexpr int kUpCol = 128;               // up accumulator column offset (gate at 0)
-constexpr int kSmemMax = 232448;          // 227 KB opt-in shared memory per CTA
-constexpr int kSmemReserve = 1024 + 256;  // alignment slack + barriers
-constexpr int kMaxStages = 8;
+constexpr int kBK = 64;                  // K elements per smem stage: one 128-byte swizzle row
+constexpr int kTokM = 128;               // MMA M: token rows (the tile's n, rest unused)
+constexpr int kWRows = 256;              // MMA N: weight rows per MMA
+constexpr int kRowsA = 128;              // gate/up tile: rows of gate and of up
+constexpr int kRowsB = 256;              // down tile: rows of Wd (= rows of H)
+constexpr int kNMaxA = kTokM;            // tokens per gate/up tile
+constexpr int kNMaxB = 64;               // tokens per down tile (act_hi + act_lo rows <= 128)
+constexpr int kRowB = kBK * 2;           // bytes of one row per stage
+constexpr int kWBox = 128;               // weight rows per TMA box
+constexpr int kBoxRows = 16;             // token rows per TMA box
+constexpr int kWStageBytes = kWRows * kRowB;  // 32 KB
+constexpr int kTokBytes = kTokM * kRowB;      // 16 KB: the rows one MMA reads as A
+constexpr int kGemmThreads = 224;        // 7 warps
+constexpr int kTmemCols = 512;           // two accumulator buffers of 256 columns
+constexpr int kAccStride = 256;          // columns between accumulator buffers
+constexpr int kSmemMax = 232448;         // 227 KB opt-in shared memory per CTA
+constexpr int kStagePitch = 17;          // down epilogue: floats per parked token (16 + pad)
+constexpr int kXchgBytes = kNMaxB * kStagePitch * 4;
+constexpr int kSmemReserve = 1024 + 512 + kXchgBytes;  // alignment slack, barriers, exchange
+constexpr int kMaxWStages = 8;           // weight ring depth limit
+constexpr int kMaxTStages = 4;           // token ring depth limit
+constexpr int kJMax = 4;                 // down: partial sums per output tile, at most
 
 // Bucket metadata (int32 words in the workspace), written by k_bucket:
-//   [0] rows in use, [1] gate/up items, [2] down items,
-//   cnt[E], base[E], ntl[E] (token tiles), preA[E+1], preB[E+1] from word 16.
+//   [0] rows in use, [1] gate/up tiles, [2] down tiles, and from word 16
+//   cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
+//   preA[E+1], preB[E+1] (tiles before each expert).
 constexpr int kMetaHdr = 16;
-__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 5 * E + 2; }
+__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 6 * E + 2; }
 struct MetaView {
   const int* cnt;
   const int* base;
-  const int* ntl;
+  const int* ntlA;
+  const int* ntlB;
   const int* preA;
   const int* preB;
 };
@@ -79,8 +94,9 @@ __host__ __device__ inline MetaView meta_view(const int* m, int E) {
   MetaView v;
   v.cnt = m + kMetaHdr;
   v.base = v.cnt + E;
-  v.ntl = v.base + E;
-  v.preA = v.ntl + E;
+  v.ntlA = v.base + E;
+  v.ntlB = v.ntlA + E;
+  v.preA = v.ntlB + E;
   v.preB = v.preA + E + 1;
   return v;
 }
@@ -100,9 +116,10 @@ WR_DEVINL uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor of kind::f16: bf16 A and B, fp32 accumulator, both
-// K-major, M = 128, N = n (multiple of 16, 16..256).
-WR_DEVINL uint32_t idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+// K-major, M = m (64 or 128), N = n (multiple of 16, 16..256).
+WR_DEVINL uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
 }
 
 WR_DEVINL void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -189,6 +206,21 @@ WR_DEVINL void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, in
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Named barrier `id` over `n` threads that also ORs `v` across them: every
+// participant gets the same answer, so a decision taken on it is uniform.
+WR_DEVINL bool named_bar_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -201,17 +233,20 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 // row: expert e's rows are base[e] .. base[e] + cnt[e] - 1 in ascending
 // token order, followed by zero-weight padding up to a multiple of 16.
 // Pairs of other ranks' experts get slot -1.  Also writes the tile counts
-// the GEMM kernels walk: per expert ntl token tiles of <= nmax rows,
-// mtA * ntl gate/up items and mtB * S * ntl down items.
+// the GEMM kernels walk: per expert ntlA (ntlB) token tiles of <= nmaxA
+// (nmaxB) rows, mtA * ntlA gate/up tiles and mtB * ntlB down tiles.
 __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
-                                                 const float* __restrict__ w, int TK, int K,
-                                                 int ep_first, int E, int nmax, int mtA, int mtB,
-                                                 int S, int* __restrict__ meta,
-                                                 int32_t* __restrict__ slot,
-                                                 int32_t* __restrict__ row_tok,
-                                                 float* __restrict__ row_w) {
+                                                const float* __restrict__ w, int TK, int K,
+                                                int ep_first, int E, int nmaxA, int nmaxB,
+                                                int mtA, int mtB, int* __restrict__ meta,
+                                                int32_t* __restrict__ slot,
+                                                int32_t* __restrict__ row_tok,
+                                                int32_t* __restrict__ row_e,
+                                                float* __restrict__ row_w) {
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_base[kMaxExperts];
+  griddep_wait();
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
     const int e = ids[i] - ep_first;
@@ -227,26 +262,28 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    MetaView v = meta_view(meta, E);
-    int* cnt = const_cast<int*>(v.cnt);
-    int* base = const_cast<int*>(v.base);
-    int* ntl = const_cast<int*>(v.ntl);
-    int* preA = const_cast<int*>(v.preA);
-    int* preB = const_cast<int*>(v.preB);
+    int* cnt = meta + kMetaHdr;
+    int* base = cnt + E;
+    int* ntlA = base + E;
+    int* ntlB = ntlA + E;
+    int* preA = ntlB + E;
+    int* preB = preA + E + 1;
     int b = 0, pa = 0, pb = 0;
     for (int e = 0; e < E; ++e) {
       const int n = s_cnt[e];
       const int np = (n + 15) & ~15;
-      const int nt = (np + nmax - 1) / nmax;
+      const int na = (np + nmaxA - 1) / nmaxA;
+      const int nb = (np + nmaxB - 1) / nmaxB;
       cnt[e] = n;
       base[e] = b;
       s_base[e] = b;
-      ntl[e] = nt;
+      ntlA[e] = na;
+      ntlB[e] = nb;
       preA[e] = pa;
       preB[e] = pb;
       b += np;
-      pa += mtA * nt;
-      pb += mtB * S * nt;
+      pa += mtA * na;
+      pb += mtB * nb;
     }
     preA[E] = pa;
     preB[E] = pb;
@@ -264,6 +301,7 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
         const int r = run + __popc(bal & ((1u << lane) - 1u));
         slot[j + lane] = r;
         row_tok[r] = (j + lane) / K;
+        row_e[r] = e;
         row_w[r] = w[j + lane];
       }
       run += __popc(bal);
@@ -271,6 +309,7 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
     const int end = s_base[e] + ((s_cnt[e] + 15) & ~15);
     for (int r = run + lane; r < end; r += 32) {
       row_tok[r] = -1;
+      row_e[r] = e;
       row_w[r] = 0.0f;
     }
   }
@@ -281,6 +320,8 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
                                                 const int* __restrict__ meta,
                                                 const int32_t* __restrict__ row_tok,
                                                 uint4* __restrict__ xg) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int rows = meta[0];
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const int t = row_tok[r];
@@ -294,27 +335,69 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
   }
 }
 
-// out[t, :] = sum over k of (slot >= 0 ? sum over splits of Y[split][slot] : 0),
-// k and splits ascending.
+// ---------------------------------------------------------------------------
+// Down-projection work split (stream-K): the down tiles' K chunks, laid end
+// to end (tile-major), are cut into G equal ranges, one per CTA.  A tile
+// whose chunks straddle several ranges gets one fp32 partial per CTA that
+// touched it, written to partial slot j = CTA - first CTA of the tile; the
+// combine adds a tile's partials in slot order.  G is capped so that every
+// range holds at least ceil(kc / (kJMax - 1)) chunks, which bounds the
+// partials per tile by kJMax.
+// ---------------------------------------------------------------------------
+struct SplitK {
+  int64_t U;  // chunks in total
+  int G;      // CTAs with work
+  int kc;     // chunks per tile
+  // CTA whose range holds chunk u: the largest c with floor(c U / G) <= u.
+  WR_DEVINL int cta_of(int64_t u) const { return (int)(((u + 1) * G - 1) / U); }
+};
+
+WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid) {
+  SplitK s;
+  s.U = (int64_t)tiles * kc;
+  s.kc = kc;
+  const int L = (kc + kJMax - 2) / (kJMax - 1);
+  int64_t g = s.U / L;
+  if (g < 1) g = 1;
+  if (g > grid) g = grid;
+  s.G = (int)g;
+  return s;
+}
+
+// out[t, :] = sum over k ascending of (slot >= 0 ? sum over the tile's
+// partials in slot order : 0).  One fixed order: deterministic.
 __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypart,
-                                                 const int32_t* __restrict__ slot, int K, int H4,
-                                                 int S, int rmax, float4* __restrict__ out) {
+                                                 const int32_t* __restrict__ slot,
+                                                 const int32_t* __restrict__ row_e,
+                                                 const int* __restrict__ meta, int E, int K,
+                                                 int H4, int rmax, int kcB, int nmaxB, int grid,
+                                                 float4* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int t = blockIdx.x;
-  for (int h = threadIdx.x; h < H4; h += blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < K; ++k) {
-      const int r = slot[(int64_t)t * K + k];
-      if (r < 0) continue;
-      for (int s = 0; s < S; ++s) {
-        const float4 v = ypart[((int64_t)s * rmax + r) * H4 + h];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
+  const int h = blockIdx.y * blockDim.x + threadIdx.x;
+  if (h >= H4) return;
+  const MetaView mv = meta_view(meta, E);
+  const SplitK sk = make_splitk(meta[2], kcB, grid);
+  const int mt = (h * 4) / kRowsB;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < K; ++k) {
+    const int r = slot[(int64_t)t * K + k];
+    if (r < 0) continue;
+    const int e = row_e[r];
+    const int nt = (r - mv.base[e]) / nmaxB;
+    const int64_t tile = (int64_t)mv.preB[e] + (int64_t)mt * mv.ntlB[e] + nt;
+    const int c0 = sk.cta_of(tile * kcB);
+    const int c1 = sk.cta_of((tile + 1) * kcB - 1);
+    for (int j = 0; j <= c1 - c0; ++j) {
+      const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
     }
-    out[(int64_t)t * H4 + h] = acc;
   }
+  out[(int64_t)t * H4 + h] = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -323,88 +406,173 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
 
 struct GemmArgs {
   const int* meta;
-  int E;            // experts of this rank
+  int E;               // experts of this rank
   int H, I;
-  int nmax;         // token rows per tile
-  int S;            // down: K splits
-  int kc_total;     // K chunks of kBK (gate/up: over H, down: over I)
-  int kc_split;     // down: chunks per split
-  int mt;           // weight-row tiles per expert
-  int rmax;         // rows of one activation half (lo rows start at rmax)
-  int stages;
-  int stage_bytes;
+  int nmax;            // token rows per tile
+  int kc_total;        // K chunks of kBK per tile (gate/up: over H, down: over I)
+  int rmax;            // rows of one activation half (lo rows start at rmax)
+  int wstages, tstages;  // weight ring / token ring depth
+  int tstage_bytes;      // token slot: gate/up nmax rows, down 2 * nmax rows
   const float* row_w;  // gate/up epilogue: per-row routing weight
   uint16_t* act;       // gate/up output: [2][rmax][I] bf16 (hi, lo)
-  float* ypart;        // down output: [S][rmax][H] fp32
+  float* ypart;        // down output: [kJMax][rmax][H] fp32
   uint32_t* status;
 };
 
-struct Item {
-  int e, m0, row0, n, kc0, kc1, s;
+// One unit of a CTA's work: weight rows starting at m0 (gate/up: rows
+// m0..m0+127 of gate and of up; down: rows m0..m0+255 of Wd) of expert e
+// against token rows [row0, row0 + n), K chunks [kc0, kc1) taken in the
+// rotated order kc0 + (rot + i) % (kc1 - kc0); j = partial slot (down).
+// The rotation depends only on the tile, so the summation order is fixed;
+// it spreads the CTAs that share a token tile over different K chunks, so
+// they do not all fetch the same L2 lines at the same moment.
+struct Work {
+  int e, m0, row0, n, kc0, kc1, rot, j;
+  WR_DEVINL int kc_at(int i) const {
+    const int len = kc1 - kc0;
+    int k = rot + i;
+    if (k >= len) k -= len;
+    return kc0 + k;
+  }
 };
 
-// Item i of this phase: experts in order; inside an expert the token tile
-// varies fastest (tiles that share a weight tile run on neighbouring CTAs at
-// the same time, so the second read of the weights mostly hits L2), then the
-// K split (down), then the weight-row tile.  `e` is advanced monotonically:
-// each role walks its items in increasing order.
+// The sequence of work one CTA runs; every role of the CTA walks the same
+// sequence.  Gate/up: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (each
+// whole).  Down: this CTA's stream-K chunk range.  Tiles are numbered
+// expert-major; inside an expert the token tile varies fastest (tiles that
+// share weights run on neighbouring CTAs at the same time, so the second
+// read mostly hits L2), then the weight-row tile.
 template <bool kGU>
-WR_DEVINL Item decode_item(const GemmArgs& a, const MetaView& mv, int i, int& e) {
-  const int* pre = kGU ? mv.preA : mv.preB;
-  while (e + 1 < a.E && __ldg(pre + e + 1) <= i) ++e;
-  const int local = i - __ldg(pre + e);
-  const int nt = __ldg(mv.ntl + e);
-  const int tn = local % nt;
-  const int rest = local / nt;
-  Item it;
-  it.e = e;
-  int mtile;
-  if (kGU) {
-    it.s = 0;
-    mtile = rest;
-    it.kc0 = 0;
-    it.kc1 = a.kc_total;
-  } else {
-    it.s = rest % a.S;
-    mtile = rest / a.S;
-    it.kc0 = it.s * a.kc_split;
-    it.kc1 = min(a.kc_total, it.kc0 + a.kc_split);
+struct WorkIter {
+  int i, total;
+  int64_t u, u1;
+  int e;
+  SplitK sk;
+
+  WR_DEVINL bool init(const GemmArgs& a) {
+    e = 0;
+    if (kGU) {
+      i = blockIdx.x;
+      total = __ldg(a.meta + 1);
+      return i < total;
+    }
+    sk = make_splitk(__ldg(a.meta + 2), a.kc_total, gridDim.x);
+    if (sk.U == 0 || (int)blockIdx.x >= sk.G) return false;
+    u = (int64_t)blockIdx.x * sk.U / sk.G;
+    u1 = (int64_t)(blockIdx.x + 1) * sk.U / sk.G;
+    return u < u1;
   }
-  it.m0 = mtile * kBM;
-  const int np = (__ldg(mv.cnt + e) + 15) & ~15;
-  it.row0 = __ldg(mv.base + e) + tn * a.nmax;
-  it.n = min(a.nmax, np - tn * a.nmax);
-  return it;
-}
+
+  WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
+    int tile;
+    if (kGU) {
+      if (i >= total) return false;
+      tile = i;
+      i += gridDim.x;
+      w.kc0 = 0;
+      w.kc1 = a.kc_total;
+      w.j = 0;
+    } else {
+      if (u >= u1) return false;
+      tile = (int)(u / sk.kc);
+      const int kc0 = (int)(u - (int64_t)tile * sk.kc);
+      const int64_t room = u1 - u;
+      const int len = (int64_t)(sk.kc - kc0) < room ? sk.kc - kc0 : (int)room;
+      w.kc0 = kc0;
+      w.kc1 = kc0 + len;
+      w.j = (int)blockIdx.x - sk.cta_of((int64_t)tile * sk.kc);
+      u += len;
+    }
+    const int* pre = kGU ? mv.preA : mv.preB;
+    const int* ntl = kGU ? mv.ntlA : mv.ntlB;
+    while (e + 1 < a.E && __ldg(pre + e + 1) <= tile) ++e;
+    const int local = tile - __ldg(pre + e);
+    const int nt = __ldg(ntl + e);
+    const int tn = local % nt;
+    w.e = e;
+    w.m0 = (local / nt) * (kGU ? kRowsA : kRowsB);
+    const int np = (__ldg(mv.cnt + e) + 15) & ~15;
+    w.row0 = __ldg(mv.base + e) + tn * a.nmax;
+    w.n = min(a.nmax, np - tn * a.nmax);
+    w.rot = (int)(((unsigned)tile * 37u) % (unsigned)(w.kc1 - w.kc0));
+    return true;
+  }
+};
 
 WR_DEVINL void flag_timeout(const GemmArgs& a, volatile int* abort, uint32_t bit) {
   *abort = 1;
   atomicOr(a.status, bit);
 }
 
+// Waits until the last arming of each of the `stages` barriers (armed
+// `issued` times in ring order) has completed: the copies they count must
+// land before this CTA's shared memory is released.
+WR_DEVINL void drain_ring(uint64_t* full, int stages, uint32_t issued, uint32_t* status) {
+  for (int s = 0; s < stages; ++s) {
+    const uint32_t n_s = issued / stages + ((uint32_t)s < issued % stages ? 1u : 0u);
+    if (n_s == 0) continue;
+    if (!mbar_wait(&full[s], (n_s - 1u) & 1u, nullptr)) {
+      atomicOr(status, DEV_TIMEOUT_DRAIN);
+      return;
+    }
+  }
+}
+
+// SiLU with the fast exponential and division intrinsics (a few ulp).
+WR_DEVINL float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+WR_DEVINL uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
+  return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// D[token, weight row] = tokens (MMA A: M = 128 token rows, of which the
+// tile's n are loaded; the rest of the smem tile is stale and only feeds
+// accumulator lanes nobody reads) x weights (MMA B: N = 256 weight rows).
+// Each MMA takes 256 weight rows x 16 K, whatever the token count.
+//
+// gate/up: B rows 0..127 = gate rows m0.., 128..255 = up rows m0.., so
+//   accumulator lane t (token) holds gate and up of the same rows in columns
+//   c and 128 + c: SwiGLU runs in the thread that owns the token.
+// down:    A rows 0..63 = act_hi of the tile's tokens, 64..127 = act_lo, so
+//   lane t and lane 64 + t hold the two halves of token t's output.
+//
+// Warp roles: 0 weight loads, 6 token loads (one elected lane each), 1 TMEM
+// owner + MMA issue (one elected lane), 2..5 epilogue (TMEM lane quarter
+// warp % 4).  Weights and tokens have separate smem rings: weights come from
+// HBM and need a deep ring, token tiles come from L2 and a shallow one does.
 template <bool kGU>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_b, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  const int total = __ldg(a.meta + (kGU ? 1 : 2));
-  if ((int)blockIdx.x >= total) return;  // whole CTA: no work
+  griddep_launch_dependents();
 
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
+  // [token ring][weight ring][barriers, exchange]: a token slot may be
+  // shorter than the 128 rows an MMA reads as A; the overhang reads the
+  // following slots or the weight ring (stale rows, unread accumulator lanes).
+  uint8_t* tring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * a.stage_bytes);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* tfull = empty + kMaxStages;  // [2]
-  uint64_t* tempty = tfull + 2;          // [2]
-  uint64_t* drain = tempty + 2;          // [1]
+  uint8_t* smem = tring + (size_t)a.tstages * a.tstage_bytes;
+  uint64_t* fullW = reinterpret_cast<uint64_t*>(smem + (size_t)a.wstages * kWStageBytes);
+  uint64_t* emptyW = fullW + kMaxWStages;
+  uint64_t* fullT = emptyW + kMaxWStages;
+  uint64_t* emptyT = fullT + kMaxTStages;
+  uint64_t* tfull = emptyT + kMaxTStages;  // [2]
+  uint64_t* tempty = tfull + 2;            // [2]
+  uint64_t* drain = tempty + 2;            // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(fullW) + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < a.wstages; ++s) {
+      mbar_init(&fullW[s], 1);
+      mbar_init(&emptyW[s], 1);
+    }
+    for (int s = 0; s < a.tstages; ++s) {
+      mbar_init(&fullT[s], 1);
+      mbar_init(&emptyT[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -416,6 +584,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_b);
   }
+  // Everything above touches only this CTA; the previous kernel's outputs
+  // (bucket metadata, gathered tokens, activations) are read from here on.
+  griddep_wait();
+  {
+    WorkIter<kGU> probe;
+    if (!probe.init(a)) return;  // whole CTA: no work (uniform)
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -426,75 +601,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const MetaView mv = meta_view(a.meta, a.E);
 
-  if (warp == 0) {
-    // ---- TMA producer ----
+  if (warp == 0 || warp == 6) {
+    // ---- TMA producers: warp 0 weights, warp 6 token tiles ----
     if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_b = l2_policy_evict_last();
+      const bool wprod = warp == 0;
+      const uint64_t pol = wprod ? l2_policy_evict_first() : l2_policy_evict_last();
+      uint64_t* full = wprod ? fullW : fullT;
+      uint64_t* empty = wprod ? emptyW : emptyT;
+      const int stages = wprod ? a.wstages : a.tstages;
+      uint8_t* ring = wprod ? smem : tring;
+      const int sbytes = wprod ? kWStageBytes : a.tstage_bytes;
       int st = 0;
       uint32_t ph = 0;
       uint32_t issued = 0;
-      int e = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < total; i += gridDim.x) {
-        const Item it = decode_item<kGU>(a, mv, i, e);
-        const int nbox = it.n / kBoxRows;
-        const uint32_t bytes = (kGU ? 2 : 1) * kTileA + (kGU ? 1 : 2) * it.n * kRowB;
-        for (int kc = it.kc0; kc < it.kc1; ++kc) {
+      WorkIter<kGU> it;
+      it.init(a);
+      Work w;
+      while (ok && it.next(a, mv, w)) {
+        const int nbox = w.n / kBoxRows;
+        const uint32_t bytes =
+            wprod ? (uint32_t)kWStageBytes : (uint32_t)((kGU ? 1 : 2) * w.n * kRowB);
+        for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+          const int kc = w.kc_at(i);
           if (!mbar_wait(&empty[st], ph ^ 1u, abort)) {
             if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_EMPTY);
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[st], bytes);
-          uint8_t* sa = smem + (size_t)st * a.stage_bytes;
+          uint8_t* s = ring + (size_t)st * sbytes;
           const int kx = kc * kBK;
-          if (kGU) {
-            tma_load_3d(sa, &tm_w, kx, it.m0, it.e, &full[st], pol_w);
-            tma_load_3d(sa + kTileA, &tm_w, kx, a.I + it.m0, it.e, &full[st], pol_w);
-            uint8_t* sb = sa + 2 * kTileA;
-            for (int r = 0; r < nbox; ++r)
-              tma_load_2d(sb + r * kBoxRows * kRowB, &tm_b, kx, it.row0 + r * kBoxRows, &full[st],
-                          pol_b);
+          if (wprod) {
+            // gate/up: gate rows m0.. then up rows m0..; down: Wd rows m0..m0+255
+            tma_load_3d(s, &tm_w, kx, w.m0, w.e, &full[st], pol);
+            tma_load_3d(s + kWBox * kRowB, &tm_w, kx, kGU ? a.I + w.m0 : w.m0 + kWBox, w.e,
+                        &full[st], pol);
           } else {
-            tma_load_3d(sa, &tm_w, kx, it.m0, it.e, &full[st], pol_w);
-            uint8_t* sh = sa + kTileA;
-            uint8_t* sl = sh + a.nmax * kRowB;
-            for (int r = 0; r < nbox; ++r) {
-              tma_load_2d(sh + r * kBoxRows * kRowB, &tm_b, kx, it.row0 + r * kBoxRows, &full[st],
-                          pol_b);
-              tma_load_2d(sl + r * kBoxRows * kRowB, &tm_b, kx, a.rmax + it.row0 + r * kBoxRows,
-                          &full[st], pol_b);
+            for (int r = 0; r < nbox; ++r)
+              tma_load_2d(s + r * kBoxRows * kRowB, &tm_b, kx, w.row0 + r * kBoxRows, &full[st],
+                          pol);
+            if (!kGU) {  // act_lo rows at tile rows nmax..
+              uint8_t* sl = s + a.nmax * kRowB;
+              for (int r = 0; r < nbox; ++r)
+                tma_load_2d(sl + r * kBoxRows * kRowB, &tm_b, kx, a.rmax + w.row0 + r * kBoxRows,
+                            &full[st], pol);
             }
           }
           ++issued;
-          if (++st == a.stages) {
+          if (++st == stages) {
             st = 0;
             ph ^= 1u;
           }
         }
       }
-      // Drain: the last arming of each stage must have landed before this
-      // CTA's shared memory can be released.
-      for (int s = 0; s < a.stages; ++s) {
-        const uint32_t n_s = issued / a.stages + ((uint32_t)s < issued % a.stages ? 1u : 0u);
-        if (n_s == 0) continue;
-        if (!mbar_wait(&full[s], (n_s - 1u) & 1u, nullptr)) {
-          atomicOr(a.status, DEV_TIMEOUT_DRAIN);
-          break;
-        }
-      }
+      drain_ring(full, stages, issued, a.status);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      int st = 0;
-      uint32_t ph = 0;
+      int sw = 0, stt = 0;
+      uint32_t phw = 0, pht = 0;
       int j = 0;
-      int e = 0;
       bool ok = true;
-      for (int i = blockIdx.x; ok && i < total; i += gridDim.x, ++j) {
-        const Item it = decode_item<kGU>(a, mv, i, e);
+      const uint32_t idesc = idesc_bf16(kTokM, kWRows);
+      WorkIter<kGU> it;
+      it.init(a);
+      Work w;
+      for (; ok && it.next(a, mv, w); ++j) {
         const int ab = j & 1;
         const uint32_t aph = (uint32_t)(j >> 1) & 1u;
         if (!mbar_wait(&tempty[ab], aph ^ 1u, abort)) {
@@ -503,34 +677,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(ab * kAccStride);
-        const uint32_t idesc = idesc_bf16(it.n);
-        for (int kc = it.kc0; kc < it.kc1; ++kc) {
-          if (!mbar_wait(&full[st], ph, abort)) {
+        for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+          if (!mbar_wait(&fullW[sw], phw, abort) || !mbar_wait(&fullT[stt], pht, abort)) {
             if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + (size_t)st * a.stage_bytes);
+          const uint32_t sw_addr = smem_u32(smem + (size_t)sw * kWStageBytes);
+          const uint32_t st_addr = smem_u32(tring + (size_t)stt * a.tstage_bytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint32_t acc = (kc > it.kc0 || kk > 0) ? 1u : 0u;
-            if (kGU) {
-              const uint64_t bdesc = sw128_desc(sa + 2 * kTileA + kk * 32);
-              umma_bf16(d, sw128_desc(sa + kk * 32), bdesc, idesc, acc);
-              umma_bf16(d + kUpCol, sw128_desc(sa + kTileA + kk * 32), bdesc, idesc, acc);
-            } else {
-              const uint64_t adesc = sw128_desc(sa + kk * 32);
-              const uint32_t sh = sa + kTileA;
-              const uint32_t sl = sh + a.nmax * kRowB;
-              umma_bf16(d, adesc, sw128_desc(sh + kk * 32), idesc, acc);
-              umma_bf16(d, adesc, sw128_desc(sl + kk * 32), idesc, 1u);
-            }
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            umma_bf16(d, sw128_desc(st_addr + kk * 32), sw128_desc(sw_addr + kk * 32), idesc, acc);
           }
-          umma_commit(&empty[st]);
-          if (++st == a.stages) {
-            st = 0;
-            ph ^= 1u;
+          umma_commit(&emptyW[sw]);
+          umma_commit(&emptyT[stt]);
+          if (++sw == a.wstages) {
+            sw = 0;
+            phw ^= 1u;
+          }
+          if (++stt == a.tstages) {
+            stt = 0;
+            pht ^= 1u;
           }
         }
         if (!ok) break;
@@ -543,55 +712,98 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---- epilogue: warps 2..5, TMEM lane quarter warp % 4 ----
     const int q = warp & 3;
-    const int rloc = 32 * q + lane;
     int j = 0;
-    int e = 0;
-    for (int i = blockIdx.x; i < total; i += gridDim.x, ++j) {
-      if (*abort) break;
-      const Item it = decode_item<kGU>(a, mv, i, e);
+    WorkIter<kGU> it;
+    it.init(a);
+    Work w;
+    for (; it.next(a, mv, w); ++j) {
       const int ab = j & 1;
       const uint32_t aph = (uint32_t)(j >> 1) & 1u;
-      if (!mbar_wait(&tfull[ab], aph, abort)) {
+      bool bad = *abort != 0;
+      if (!bad && !mbar_wait(&tfull[ab], aph, abort)) {
         if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_ACT);
-        break;
+        bad = true;
       }
+      // The four epilogue warps leave together or not at all: the down
+      // epilogue synchronises them on a named barrier.
+      if (named_bar_or(2, 128, bad)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kAccStride);
       if (kGU) {
-        const int irow = it.m0 + rloc;
-        const bool inb = irow < a.I;
-        __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(a.act);
-        __nv_bfloat16* lo = hi + (int64_t)a.rmax * a.I;
-        for (int c0 = 0; c0 < it.n; c0 += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(taddr + c0, g);
-          tmem_ld16(taddr + kUpCol + c0, u);
-          tmem_wait_ld(g);
-          reg_dep16(u);
+        // lane = token t of the tile; columns c / 128 + c = gate / up row m0 + c
+        const int t = 32 * q + lane;
+        if (32 * q < w.n) {  // warp-uniform: this quarter holds tokens
+          const bool live = t < w.n;
+          const int r = w.row0 + t;
+          const float wt = live ? __ldg(a.row_w + r) : 0.0f;
+          uint16_t* hi = a.act + (int64_t)r * a.I;
+          uint16_t* lo = hi + (int64_t)a.rmax * a.I;
+          for (int c0 = 0; c0 < kRowsA; c0 += 16) {
+            uint32_t g[16], u[16];
+            tmem_ld16(taddr + c0, g);
+            tmem_ld16(taddr + kRowsA + c0, u);
+            tmem_wait_ld(g);
+            reg_dep16(u);
+            uint32_t ph[8], pl[8];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int r = it.row0 + c0 + c;
-            const float wv = __ldg(a.row_w + r);
-            const float av = silu(__uint_as_float(g[c])) * __uint_as_float(u[c]) * wv;
-            const __nv_bfloat16 h = __float2bfloat16_rn(av);
-            const __nv_bfloat16 l = __float2bfloat16_rn(av - __bfloat162float(h));
-            if (inb) {
-              hi[(int64_t)r * a.I + irow] = h;
-              lo[(int64_t)r * a.I + irow] = l;
+            for (int c = 0; c < 16; c += 2) {
+              float av[2];
+#pragma unroll
+              for (int k = 0; k < 2; ++k)
+                av[k] = silu_fast(__uint_as_float(g[c + k])) * __uint_as_float(u[c + k]) * wt;
+              const __nv_bfloat16 h0 = __float2bfloat16_rn(av[0]);
+              const __nv_bfloat16 h1 = __float2bfloat16_rn(av[1]);
+              ph[c / 2] = pack_bf16x2(h0, h1);
+              pl[c / 2] = pack_bf16x2(__float2bfloat16_rn(av[0] - __bfloat162float(h0)),
+                                      __float2bfloat16_rn(av[1] - __bfloat162float(h1)));
+            }
+            const int i = w.m0 + c0;
+            if (live) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                if (i + 8 * h < a.I) {
+                  *reinterpret_cast<uint4*>(hi + i + 8 * h) =
+                      make_uint4(ph[4 * h], ph[4 * h + 1], ph[4 * h + 2], ph[4 * h + 3]);
+                  *reinterpret_cast<uint4*>(lo + i + 8 * h) =
+                      make_uint4(pl[4 * h], pl[4 * h + 1], pl[4 * h + 2], pl[4 * h + 3]);
+                }
             }
           }
         }
       } else {
-        const int hrow = it.m0 + rloc;
-        const bool inb = hrow < a.H;
-        float* yp = a.ypart + (int64_t)it.s * a.rmax * a.H;
-        for (int c0 = 0; c0 < it.n; c0 += 16) {
+        // lanes 0..nmax-1: act_hi part of the tile's tokens, lanes nmax..:
+        // act_lo part.  Threads holding a lo part park it in smem; the
+        // thread holding the hi part of the same token adds and stores 16
+        // consecutive outputs.
+        const int L = 32 * q + lane;                  // accumulator lane
+        const bool lo_lane = L >= a.nmax && L < a.nmax + w.n;
+        const bool hi_lane = L < w.n;
+        const bool has = 32 * q < a.nmax + w.n;      // warp-uniform: some lane is used
+        float* park = xchg + (lo_lane ? L - a.nmax : (hi_lane ? L : 0)) * kStagePitch;
+        float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + L) * a.H;
+        for (int c0 = 0; c0 < kWRows; c0 += 16) {
           uint32_t v[16];
-          tmem_ld16(taddr + c0, v);
-          tmem_wait_ld(v);
+          if (has) {
+            tmem_ld16(taddr + c0, v);
+            tmem_wait_ld(v);
+            if (lo_lane) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            if (inb) yp[(int64_t)(it.row0 + c0 + c) * a.H + hrow] = __uint_as_float(v[c]);
+              for (int c = 0; c < 16; ++c) park[c] = __uint_as_float(v[c]);
+            }
+          }
+          named_bar_sync(1, 128);
+          if (hi_lane) {
+            const int h = w.m0 + c0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (h + 4 * k < a.H)
+                *reinterpret_cast<float4*>(yrow + h + 4 * k) =
+                    make_float4(__uint_as_float(v[4 * k]) + park[4 * k],
+                                __uint_as_float(v[4 * k + 1]) + park[4 * k + 1],
+                                __uint_as_float(v[4 * k + 2]) + park[4 * k + 2],
+                                __uint_as_float(v[4 * k + 3]) + park[4 * k + 3]);
+          }
+          named_bar_sync(1, 128);
         }
       }
       tc_fence_before();
@@ -652,66 +864,75 @@ size_t a256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Everything the grouped path derives from the problem on the host.
 struct GroupedPlan {
-  int nmax;       // token rows per tile
-  int rmax;       // row capacity (>= padded rows in use)
-  int mtA, mtB;   // weight-row tiles per expert (gate/up over I, down over H)
-  int kcA, kcB;   // K chunks (over H, over I)
-  int S, kc_split;
-  int stagesA, stagesB, stage_bytesA, stage_bytesB;
-  size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_rw, off_xg, off_act, off_y, total;
+  int nmaxA, nmaxB;  // token rows per tile
+  int rmax;          // row capacity (>= padded rows in use)
+  int mtA, mtB;      // weight-row tiles per expert (gate/up over I, down over H)
+  int kcA, kcB;      // K chunks (over H, over I)
+  int wstA, tstA, tbA;  // gate/up rings: weight depth, token depth, token slot bytes
+  int wstB, tstB, tbB;  // down rings
+  size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_re, off_rw, off_xg, off_act, off_y,
+      total;
 };
 
-int split_count(int kcB, int units, int sms) {
-  int best = 1;
-  double best_eff = 0.0;
-  for (int s = 1; s <= 8; ++s) {
-    if (s > 1 && kcB / s < 8) break;
-    const int items = units * s;
-    const int rounds = (items + sms - 1) / sms;
-    const double eff = (double)items / ((double)rounds * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = s;
-    }
-  }
-  return best;
+// Ring depths: token slots (from L2) get up to 48 KB in 2..4 slots, the
+// weights (from HBM) every remaining byte, up to kMaxWStages.
+void ring_split(int tbytes, int* wst, int* tst) {
+  int t = 49152 / tbytes;
+  t = t < 2 ? 2 : (t > kMaxTStages ? kMaxTStages : t);
+  int w = (kSmemMax - kSmemReserve - t * tbytes) / kWStageBytes;
+  // the last token slot's 128-row MMA window must end inside the allocation
+  static_assert(kTokBytes <= 4 * kWStageBytes, "token window overhang");
+  *tst = t;
+  *wst = w > kMaxWStages ? kMaxWStages : w;
 }
 
-GroupedPlan make_plan(const Problem& p, int sms) {
+GroupedPlan make_plan(const Problem& p) {
   GroupedPlan g;
   const int TK = p.T * p.K;
   const int n16 = (p.T + 15) & ~15;
-  g.nmax = n16 < kNMax ? n16 : kNMax;
+  g.nmaxA = n16 < kNMaxA ? n16 : kNMaxA;
+  g.nmaxB = n16 < kNMaxB ? n16 : kNMaxB;
   g.rmax = (TK + 15 * p.ep_num + 15) & ~15;
-  g.mtA = (p.I + kBM - 1) / kBM;
-  g.mtB = (p.H + kBM - 1) / kBM;
+  g.mtA = (p.I + kRowsA - 1) / kRowsA;
+  g.mtB = (p.H + kRowsB - 1) / kRowsB;
   g.kcA = (p.H + kBK - 1) / kBK;
   g.kcB = (p.I + kBK - 1) / kBK;
-  const int active = TK < p.ep_num ? TK : p.ep_num;
-  const int s0 = split_count(g.kcB, active * g.mtB, sms);
-  g.kc_split = (g.kcB + s0 - 1) / s0;
-  g.S = (g.kcB + g.kc_split - 1) / g.kc_split;
-  const int avail = kSmemMax - kSmemReserve;
-  g.stage_bytesA = 2 * kTileA + g.nmax * kRowB;
-  g.stage_bytesA = (g.stage_bytesA + 1023) & ~1023;
-  g.stage_bytesB = kTileA + 2 * g.nmax * kRowB;
-  g.stage_bytesB = (g.stage_bytesB + 1023) & ~1023;
-  g.stagesA = avail / g.stage_bytesA;
-  g.stagesB = avail / g.stage_bytesB;
-  if (g.stagesA > kMaxStages) g.stagesA = kMaxStages;
-  if (g.stagesB > kMaxStages) g.stagesB = kMaxStages;
+  g.tbA = g.nmaxA * kRowB;
+  g.tbB = 2 * g.nmaxB * kRowB;
+  ring_split(g.tbA, &g.wstA, &g.tstA);
+  ring_split(g.tbB, &g.wstB, &g.tstB);
   size_t o = kWsControlBytes;
   g.off_ids = o; o += a256(4 * (size_t)TK);
   g.off_w = o; o += a256(4 * (size_t)TK);
   g.off_slot = o; o += a256(4 * (size_t)TK);
   g.off_meta = o; o += a256(4 * (size_t)meta_words(p.ep_num));
   g.off_rtok = o; o += a256(4 * (size_t)g.rmax);
+  g.off_re = o; o += a256(4 * (size_t)g.rmax);
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
   g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
-  g.off_y = o; o += a256(4 * (size_t)g.S * g.rmax * p.H);
+  g.off_y = o; o += a256(4 * (size_t)kJMax * g.rmax * p.H);
   g.total = o;
   return g;
+}
+
+// Launches `kern` with programmatic stream serialization: it may start while
+// the previous kernel on the stream finishes, and waits for it with
+// griddep_wait() before touching its outputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 template <bool kGU>
@@ -736,20 +957,19 @@ bool grouped_supported(const Problem& p) {
          p.ep_num >= 1;
 }
 
-size_t grouped_workspace_bytes(const Problem& p) {
-  return make_plan(p, device_sm_count()).total;
-}
+size_t grouped_workspace_bytes(const Problem& p) { return make_plan(p).total; }
 
 wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, const void* wbuf,
                            float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream) {
   const int sms = device_sm_count();
-  const GroupedPlan g = make_plan(p, sms);
+  const GroupedPlan g = make_plan(p);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   int32_t* ids_d = ids ? ids : reinterpret_cast<int32_t*>(wsb + g.off_ids);
   float* w_d = w ? w : reinterpret_cast<float*>(wsb + g.off_w);
   int32_t* slot = reinterpret_cast<int32_t*>(wsb + g.off_slot);
   int* meta = reinterpret_cast<int*>(wsb + g.off_meta);
   int32_t* rtok = reinterpret_cast<int32_t*>(wsb + g.off_rtok);
+  int32_t* re = reinterpret_cast<int32_t*>(wsb + g.off_re);
   float* rw = reinterpret_cast<float*>(wsb + g.off_rw);
   uint16_t* xg = reinterpret_cast<uint16_t*>(wsb + g.off_xg);
   uint16_t* act = reinterpret_cast<uint16_t*>(wsb + g.off_act);
@@ -758,12 +978,14 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
 
   wr_status_t st = launch_router(p, x, gate_w, nullptr, ids_d, w_d, stream);
   if (st != WR_OK) return st;
-  k_bucket<<<1, 512, 0, stream>>>(ids_d, w_d, p.T * p.K, p.K, p.ep_first, p.ep_num, g.nmax,
-                                   g.mtA, g.mtB, g.S, meta, slot, rtok, rw);
+  cudaError_t ce = launch_pdl(k_bucket, dim3(1), dim3(512), 0, stream, (const int32_t*)ids_d,
+                              (const float*)w_d, p.T * p.K, p.K, p.ep_first, p.ep_num, g.nmaxA,
+                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, re, rw);
   const int gather_blocks = g.rmax < 4 * sms ? g.rmax : 4 * sms;
-  k_gather<<<gather_blocks, 256, 0, stream>>>(static_cast<const uint4*>(x), p.H / 8, meta, rtok,
-                                              reinterpret_cast<uint4*>(xg));
-  cudaError_t ce = cudaGetLastError();
+  if (ce == cudaSuccess)
+    ce = launch_pdl(k_gather, dim3(gather_blocks), dim3(256), 0, stream,
+                    static_cast<const uint4*>(x), p.H / 8, (const int*)meta,
+                    (const int32_t*)rtok, reinterpret_cast<uint4*>(xg));
   if (ce != cudaSuccess) return cuda_fail(ce, "bucket / gather launch");
 
   const Layout lay = make_layout(p.H, p.I, 2);
@@ -772,7 +994,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   {
     const cuuint64_t dims[3] = {(cuuint64_t)p.H, (cuuint64_t)2 * p.I, (cuuint64_t)p.ep_num};
     const cuuint64_t str[2] = {(cuuint64_t)p.H * 2, (cuuint64_t)lay.stride};
-    const cuuint32_t box[3] = {kBK, kBM, 1};
+    const cuuint32_t box[3] = {kBK, kWBox, 1};
     if ((st = encode_map(&tm_gu, wb + lay.off_gate, 3, dims, str, box)) != WR_OK) return st;
   }
   {
@@ -784,7 +1006,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   {
     const cuuint64_t dims[3] = {(cuuint64_t)p.I, (cuuint64_t)p.H, (cuuint64_t)p.ep_num};
     const cuuint64_t str[2] = {(cuuint64_t)p.I * 2, (cuuint64_t)lay.stride};
-    const cuuint32_t box[3] = {kBK, kBM, 1};
+    const cuuint32_t box[3] = {kBK, kWBox, 1};
     if ((st = encode_map(&tm_dn, wb + lay.off_down, 3, dims, str, box)) != WR_OK) return st;
   }
   {
@@ -801,7 +1023,6 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.E = p.ep_num;
   ga.H = p.H;
   ga.I = p.I;
-  ga.nmax = g.nmax;
   ga.rmax = g.rmax;
   ga.row_w = rw;
   ga.act = act;
@@ -809,29 +1030,33 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.status = status;
 
   GemmArgs a1 = ga;
-  a1.S = 1;
+  a1.nmax = g.nmaxA;
   a1.kc_total = g.kcA;
-  a1.kc_split = g.kcA;
-  a1.mt = g.mtA;
-  a1.stages = g.stagesA;
-  a1.stage_bytes = g.stage_bytesA;
-  const size_t smemA = (size_t)g.stagesA * g.stage_bytesA + kSmemReserve;
-  k_grouped_gemm<true><<<sms, kGemmThreads, smemA, stream>>>(tm_gu, tm_x, a1);
+  a1.wstages = g.wstA;
+  a1.tstages = g.tstA;
+  a1.tstage_bytes = g.tbA;
+  const size_t smemA = (size_t)g.wstA * kWStageBytes + (size_t)g.tstA * g.tbA + kSmemReserve;
+  ce = launch_pdl(k_grouped_gemm<true>, dim3(sms), dim3(kGemmThreads), smemA, stream, tm_gu,
+                  tm_x, a1);
+  if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (gate/up) launch");
 
   GemmArgs a2 = ga;
-  a2.S = g.S;
+  a2.nmax = g.nmaxB;
   a2.kc_total = g.kcB;
-  a2.kc_split = g.kc_split;
-  a2.mt = g.mtB;
-  a2.stages = g.stagesB;
-  a2.stage_bytes = g.stage_bytesB;
-  const size_t smemB = (size_t)g.stagesB * g.stage_bytesB + kSmemReserve;
-  k_grouped_gemm<false><<<sms, kGemmThreads, smemB, stream>>>(tm_dn, tm_act, a2);
+  a2.wstages = g.wstB;
+  a2.tstages = g.tstB;
+  a2.tstage_bytes = g.tbB;
+  const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB + kSmemReserve;
+  ce = launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream, tm_dn,
+                  tm_act, a2);
+  if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (down) launch");
 
-  k_combine<<<p.T, 256, 0, stream>>>(reinterpret_cast<const float4*>(ypart), slot, p.K, p.H / 4,
-                                     g.S, g.rmax, reinterpret_cast<float4*>(out));
-  ce = cudaGetLastError();
-  return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "grouped GEMM launch");
+  const int H4 = p.H / 4;
+  ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
+                  reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
+                  (const int32_t*)re, (const int*)meta, p.ep_num, p.K, H4, g.rmax, g.kcB,
+                  g.nmaxB, sms, reinterpret_cast<float4*>(out));
+  return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 
 }  // namespace wr
