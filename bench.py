@@ -19,6 +19,13 @@ the fused kernel's algorithmic bytes to the
 measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
 composition (restated in oracle/torch_composition.py) on a bounded sample.
 `--impl reference` times that CPU composition alone, as the reference arm.
+
+At N = 1 the line also carries `batched_sweep`: the batched-decode sweep on
+the Mixtral shape (tokens 1, 4, 16, 64, 256; router bias N(0,1) per expert to
+skew the load; 32 stacked layers with independent weights, each applied to
+the same seeded token batch), µs per layer from CUDA-graph replays of the 32
+layer calls.  Batches of two or more bf16 tokens run on the grouped
+tensor-core path (tcgen05 GEMMs over tokens bucketed per expert).
 """
 from __future__ import annotations
 
@@ -62,6 +69,10 @@ def parse():
                     help="time the layer calls eagerly instead of replaying a CUDA graph of them")
     ap.add_argument("--layers", type=int, default=0,
                     help="rotating layers (0: enough to exceed 4x L2 between reuses)")
+    ap.add_argument("--sweep-tokens", default="1,4,16,64,256",
+                    help="batched-decode sweep token counts (N = 1 only); empty: no sweep")
+    ap.add_argument("--sweep-layers", type=int, default=32)
+    ap.add_argument("--sweep-steps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -228,6 +239,83 @@ def run_reference_arm(args, world, rank):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def batched_sweep(args, dev):
+    """The batched-decode sweep (Mixtral shape, router bias, stacked layers):
+    per token count, µs per layer over CUDA-graph replays of one step (every
+    layer once) and the HBM GB/s of the distinct experts each layer streams."""
+    from warp_route import functional as F
+    from warp_route import synthetic
+
+    tokens = [int(t) for t in args.sweep_tokens.split(",") if t.strip()]
+    if not tokens:
+        return None
+    E, H, I, K = SHAPES["mixtral"]
+    nl = args.sweep_layers
+    layers = [synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, device=dev, seed=900 + li,
+                                   layer=li, router_bias=True) for li in range(nl)]
+    results = []
+    stream = torch.cuda.Stream()
+    for T in tokens:
+        gx = torch.Generator(device=dev)
+        gx.manual_seed(7000 + T)
+        x = torch.randn(T, H, generator=gx, device=dev).to(torch.bfloat16)
+        xin = x[0].contiguous() if T == 1 else x
+        distinct = []
+        for Lr in layers:
+            _, ids, _ = F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
+                                           router_bias=Lr.router_bias)
+            distinct.append(len(set(ids.cpu().view(-1).tolist())))
+
+        def step():
+            for Lr in layers:
+                if T == 1:
+                    F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
+                                       router_bias=Lr.router_bias)
+                else:
+                    F.batched_fused_moe(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
+                                        router_bias=Lr.router_bias)
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clk:
+            t0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(args.sweep_steps):
+                    g.replay()
+            t1.record(stream)
+            torch.cuda.synchronize()
+        us = t0.elapsed_time(t1) * 1000.0 / (args.sweep_steps * nl)
+        with torch.cuda.stream(stream):
+            st = F._load_extension().workspace_status(xin)
+        if st != 0:
+            raise SystemExit(f"batched sweep T={T}: device status {st}: timing discarded")
+        del g
+        mean_distinct = sum(distinct) / len(distinct)
+        wbytes = mean_distinct * 3 * H * I * 2
+        results.append({"tokens": T, "us_per_layer": round(us, 2),
+                        "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+                        "experts_per_layer": round(mean_distinct, 2),
+                        "path": "streaming kernel" if T == 1 else "grouped tcgen05 GEMMs",
+                        "clocks": clk.summary()})
+    del layers
+    torch.cuda.empty_cache()
+    return {"config": "mixtral, router bias N(0,1), bf16", "layers": nl,
+            "steps": args.sweep_steps,
+            "note": "each layer has its own weights, gate and bias and takes the same seeded "
+                    "token batch; value = µs per layer (graph replays of the layer stack); "
+                    "hbm_gbs = distinct selected experts' weight bytes / time",
+            "results": results}
 
 
 def run_ours(args, world, rank, local):
@@ -440,6 +528,10 @@ def run_ours(args, world, rank, local):
                          f"selected experts widened to fp32, median of {ncalls} after 3 warm-ups; "
                          f"warp-route's torch composition restated in oracle/torch_composition.py"}
 
+    sweep = None
+    if world == 1 and rank == 0:
+        sweep = batched_sweep(args, dev)
+
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -476,6 +568,8 @@ def run_ours(args, world, rank, local):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if sweep is not None:
+            line["batched_sweep"] = sweep
         print(json.dumps(line), flush=True)
     if comm is not None:
         torch.cuda.synchronize()

@@ -74,7 +74,8 @@ constexpr int kXchgBytes = kNMaxB * kStagePitch * 4;
 constexpr int kSmemReserve = 1024 + 512 + kXchgBytes;  // alignment slack, barriers, exchange
 constexpr int kMaxWStages = 8;           // weight ring depth limit
 constexpr int kMaxTStages = 4;           // token ring depth limit
-constexpr int kJMax = 4;                 // down: partial sums per output tile, at most
+constexpr int kJMaxA = 3;                // gate/up: CTAs sharing one tile, at most
+constexpr int kJMaxB = 4;                // down: partial sums per output tile, at most
 
 // Bucket metadata (int32 words in the workspace), written by k_bucket:
 //   [0] rows in use, [1] gate/up tiles, [2] down tiles, and from word 16
@@ -232,7 +233,8 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 // One CTA.  Pairs (t, k) whose expert is in [ep_first, ep_first + E) get a
 // row: expert e's rows are base[e] .. base[e] + cnt[e] - 1 in ascending
 // token order, followed by zero-weight padding up to a multiple of 16.
-// Pairs of other ranks' experts get slot -1.  Also writes the tile counts
+// Pairs of other ranks' experts get slot -1.  Zeroes the gate/up tile
+// counters (robust against a call that gave up half-way).  Also writes the tile counts
 // the GEMM kernels walk: per expert ntlA (ntlB) token tiles of <= nmaxA
 // (nmaxB) rows, mtA * ntlA gate/up tiles and mtB * ntlB down tiles.
 __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
@@ -242,12 +244,14 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
                                                 int32_t* __restrict__ slot,
                                                 int32_t* __restrict__ row_tok,
                                                 int32_t* __restrict__ row_e,
-                                                float* __restrict__ row_w) {
+                                                float* __restrict__ row_w,
+                                                uint32_t* __restrict__ tile_cnt, int cnt_words) {
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_base[kMaxExperts];
   griddep_wait();
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < cnt_words; i += blockDim.x) tile_cnt[i] = 0u;
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
     const int e = ids[i] - ep_first;
     if (e < 0 || e >= E) slot[i] = -1;
@@ -336,13 +340,14 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
 }
 
 // ---------------------------------------------------------------------------
-// Down-projection work split (stream-K): the down tiles' K chunks, laid end
-// to end (tile-major), are cut into G equal ranges, one per CTA.  A tile
-// whose chunks straddle several ranges gets one fp32 partial per CTA that
-// touched it, written to partial slot j = CTA - first CTA of the tile; the
-// combine adds a tile's partials in slot order.  G is capped so that every
-// range holds at least ceil(kc / (kJMax - 1)) chunks, which bounds the
-// partials per tile by kJMax.
+// Work split (stream-K), both GEMMs: the tiles' K chunks, laid end to end
+// (tile-major), are cut into G equal ranges, one per CTA.  A tile whose
+// chunks straddle several ranges is finished from partial sums: for the
+// down projection each CTA writes an fp32 partial that the combine adds (in
+// CTA order); for gate/up the partial accumulators go to a scratch buffer
+// and the last CTA to finish the tile adds them (in CTA order) and applies
+// SwiGLU.  G is capped so that every range holds at least
+// ceil(kc / (jmax - 1)) chunks, which bounds the CTAs per tile by jmax.
 // ---------------------------------------------------------------------------
 struct SplitK {
   int64_t U;  // chunks in total
@@ -350,13 +355,19 @@ struct SplitK {
   int kc;     // chunks per tile
   // CTA whose range holds chunk u: the largest c with floor(c U / G) <= u.
   WR_DEVINL int cta_of(int64_t u) const { return (int)(((u + 1) * G - 1) / U); }
+  WR_DEVINL int64_t u_lo(int c) const { return (int64_t)c * U / G; }
+  WR_DEVINL int first_cta(int tile) const { return cta_of((int64_t)tile * kc); }
+  WR_DEVINL int last_cta(int tile) const { return cta_of((int64_t)(tile + 1) * kc - 1); }
+  // 0 when `tile` is the first tile CTA c works on, else 1 (it is then c's
+  // last tile): with at most two cut tiles per CTA this names c's partials.
+  WR_DEVINL int part_slot(int c, int tile) const { return u_lo(c) / kc == tile ? 0 : 1; }
 };
 
-WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid) {
+WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid, int jmax) {
   SplitK s;
   s.U = (int64_t)tiles * kc;
   s.kc = kc;
-  const int L = (kc + kJMax - 2) / (kJMax - 1);
+  const int L = (kc + jmax - 2) / (jmax - 1);
   int64_t g = s.U / L;
   if (g < 1) g = 1;
   if (g > grid) g = grid;
@@ -378,7 +389,7 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
   const MetaView mv = meta_view(meta, E);
-  const SplitK sk = make_splitk(meta[2], kcB, grid);
+  const SplitK sk = make_splitk(meta[2], kcB, grid, kJMaxB);
   const int mt = (h * 4) / kRowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
@@ -387,8 +398,8 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
     const int e = row_e[r];
     const int nt = (r - mv.base[e]) / nmaxB;
     const int64_t tile = (int64_t)mv.preB[e] + (int64_t)mt * mv.ntlB[e] + nt;
-    const int c0 = sk.cta_of(tile * kcB);
-    const int c1 = sk.cta_of((tile + 1) * kcB - 1);
+    const int c0 = sk.first_cta((int)tile);
+    const int c1 = sk.last_cta((int)tile);
     for (int j = 0; j <= c1 - c0; ++j) {
       const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h];
       acc.x += v.x;
@@ -415,7 +426,9 @@ struct GemmArgs {
   int tstage_bytes;      // token slot: gate/up nmax rows, down 2 * nmax rows
   const float* row_w;  // gate/up epilogue: per-row routing weight
   uint16_t* act;       // gate/up output: [2][rmax][I] bf16 (hi, lo)
-  float* ypart;        // down output: [kJMax][rmax][H] fp32
+  float* ypart;        // down output: [kJMaxB][rmax][H] fp32
+  float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32
+  uint32_t* cnt;       // gate/up: CTAs done with each cut tile (zeroed by k_bucket)
   uint32_t* status;
 };
 
@@ -427,7 +440,7 @@ struct GemmArgs {
 // it spreads the CTAs that share a token tile over different K chunks, so
 // they do not all fetch the same L2 lines at the same moment.
 struct Work {
-  int e, m0, row0, n, kc0, kc1, rot, j;
+  int tile, e, m0, row0, n, kc0, kc1, rot, j;
   WR_DEVINL int kc_at(int i) const {
     const int len = kc1 - kc0;
     int k = rot + i;
@@ -444,45 +457,31 @@ struct Work {
 // read mostly hits L2), then the weight-row tile.
 template <bool kGU>
 struct WorkIter {
-  int i, total;
   int64_t u, u1;
   int e;
   SplitK sk;
 
   WR_DEVINL bool init(const GemmArgs& a) {
     e = 0;
-    if (kGU) {
-      i = blockIdx.x;
-      total = __ldg(a.meta + 1);
-      return i < total;
-    }
-    sk = make_splitk(__ldg(a.meta + 2), a.kc_total, gridDim.x);
+    sk = make_splitk(__ldg(a.meta + (kGU ? 1 : 2)), a.kc_total, gridDim.x,
+                     kGU ? kJMaxA : kJMaxB);
     if (sk.U == 0 || (int)blockIdx.x >= sk.G) return false;
-    u = (int64_t)blockIdx.x * sk.U / sk.G;
-    u1 = (int64_t)(blockIdx.x + 1) * sk.U / sk.G;
+    u = sk.u_lo(blockIdx.x);
+    u1 = sk.u_lo(blockIdx.x + 1);
     return u < u1;
   }
 
   WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
-    int tile;
-    if (kGU) {
-      if (i >= total) return false;
-      tile = i;
-      i += gridDim.x;
-      w.kc0 = 0;
-      w.kc1 = a.kc_total;
-      w.j = 0;
-    } else {
-      if (u >= u1) return false;
-      tile = (int)(u / sk.kc);
-      const int kc0 = (int)(u - (int64_t)tile * sk.kc);
-      const int64_t room = u1 - u;
-      const int len = (int64_t)(sk.kc - kc0) < room ? sk.kc - kc0 : (int)room;
-      w.kc0 = kc0;
-      w.kc1 = kc0 + len;
-      w.j = (int)blockIdx.x - sk.cta_of((int64_t)tile * sk.kc);
-      u += len;
-    }
+    if (u >= u1) return false;
+    const int tile = (int)(u / sk.kc);
+    const int kc0 = (int)(u - (int64_t)tile * sk.kc);
+    const int64_t room = u1 - u;
+    const int len = (int64_t)(sk.kc - kc0) < room ? sk.kc - kc0 : (int)room;
+    w.tile = tile;
+    w.kc0 = kc0;
+    w.kc1 = kc0 + len;
+    w.j = (int)blockIdx.x - sk.first_cta(tile);
+    u += len;
     const int* pre = kGU ? mv.preA : mv.preB;
     const int* ntl = kGU ? mv.ntlA : mv.ntlB;
     while (e + 1 < a.E && __ldg(pre + e + 1) <= tile) ++e;
@@ -494,7 +493,7 @@ struct WorkIter {
     const int np = (__ldg(mv.cnt + e) + 15) & ~15;
     w.row0 = __ldg(mv.base + e) + tn * a.nmax;
     w.n = min(a.nmax, np - tn * a.nmax);
-    w.rot = (int)(((unsigned)tile * 37u) % (unsigned)(w.kc1 - w.kc0));
+    w.rot = (int)(((unsigned)tile * 37u) % (unsigned)len);
     return true;
   }
 };
@@ -523,6 +522,32 @@ WR_DEVINL float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 WR_DEVINL uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
   return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+}
+
+// act = silu(g) * u * wt for 16 consecutive intermediate rows i.. of one
+// token, stored as bf16 hi (act rounded) and lo (act - hi rounded).
+WR_DEVINL void swiglu_store16(const float (&g)[16], const float (&u)[16], float wt, uint16_t* hi,
+                              uint16_t* lo, int i, int I) {
+  uint32_t ph[8], pl[8];
+#pragma unroll
+  for (int c = 0; c < 16; c += 2) {
+    float av[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) av[k] = silu_fast(g[c + k]) * u[c + k] * wt;
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(av[0]);
+    const __nv_bfloat16 h1 = __float2bfloat16_rn(av[1]);
+    ph[c / 2] = pack_bf16x2(h0, h1);
+    pl[c / 2] = pack_bf16x2(__float2bfloat16_rn(av[0] - __bfloat162float(h0)),
+                            __float2bfloat16_rn(av[1] - __bfloat162float(h1)));
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (i + 8 * h < I) {
+      *reinterpret_cast<uint4*>(hi + i + 8 * h) =
+          make_uint4(ph[4 * h], ph[4 * h + 1], ph[4 * h + 2], ph[4 * h + 3]);
+      *reinterpret_cast<uint4*>(lo + i + 8 * h) =
+          make_uint4(pl[4 * h], pl[4 * h + 1], pl[4 * h + 2], pl[4 * h + 3]);
+    }
 }
 
 // D[token, weight row] = tokens (MMA A: M = 128 token rows, of which the
@@ -732,42 +757,82 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (kGU) {
         // lane = token t of the tile; columns c / 128 + c = gate / up row m0 + c
         const int t = 32 * q + lane;
-        if (32 * q < w.n) {  // warp-uniform: this quarter holds tokens
-          const bool live = t < w.n;
-          const int r = w.row0 + t;
-          const float wt = live ? __ldg(a.row_w + r) : 0.0f;
-          uint16_t* hi = a.act + (int64_t)r * a.I;
-          uint16_t* lo = hi + (int64_t)a.rmax * a.I;
-          for (int c0 = 0; c0 < kRowsA; c0 += 16) {
-            uint32_t g[16], u[16];
-            tmem_ld16(taddr + c0, g);
-            tmem_ld16(taddr + kRowsA + c0, u);
-            tmem_wait_ld(g);
-            reg_dep16(u);
-            uint32_t ph[8], pl[8];
+        const bool has = 32 * q < w.n;  // warp-uniform: this quarter holds tokens
+        const bool live = t < w.n;
+        const int r = w.row0 + t;
+        uint16_t* hi = a.act + (int64_t)r * a.I;
+        uint16_t* lo = hi + (int64_t)a.rmax * a.I;
+        if (w.kc0 == 0 && w.kc1 == a.kc_total) {  // whole tile in this CTA
+          if (has) {
+            const float wt = live ? __ldg(a.row_w + r) : 0.0f;
+            for (int c0 = 0; c0 < kRowsA; c0 += 16) {
+              uint32_t gv[16], uv[16];
+              tmem_ld16(taddr + c0, gv);
+              tmem_ld16(taddr + kRowsA + c0, uv);
+              tmem_wait_ld(gv);
+              reg_dep16(uv);
+              float g[16], u[16];
 #pragma unroll
-            for (int c = 0; c < 16; c += 2) {
-              float av[2];
-#pragma unroll
-              for (int k = 0; k < 2; ++k)
-                av[k] = silu_fast(__uint_as_float(g[c + k])) * __uint_as_float(u[c + k]) * wt;
-              const __nv_bfloat16 h0 = __float2bfloat16_rn(av[0]);
-              const __nv_bfloat16 h1 = __float2bfloat16_rn(av[1]);
-              ph[c / 2] = pack_bf16x2(h0, h1);
-              pl[c / 2] = pack_bf16x2(__float2bfloat16_rn(av[0] - __bfloat162float(h0)),
-                                      __float2bfloat16_rn(av[1] - __bfloat162float(h1)));
+              for (int c = 0; c < 16; ++c) {
+                g[c] = __uint_as_float(gv[c]);
+                u[c] = __uint_as_float(uv[c]);
+              }
+              if (live) swiglu_store16(g, u, wt, hi, lo, w.m0 + c0, a.I);
             }
-            const int i = w.m0 + c0;
-            if (live) {
+          }
+        } else {
+          // Cut tile: park this CTA's partial sums, count it in; the last
+          // CTA of the tile adds the partials in CTA order and applies SwiGLU.
+          const SplitK& sk = it.sk;
+          float* pb = a.pbuf +
+                      (((size_t)blockIdx.x * 2 + sk.part_slot(blockIdx.x, w.tile)) * a.nmax + t) *
+                          kWRows;
+          if (has) {
+            for (int c0 = 0; c0 < kWRows; c0 += 16) {
+              uint32_t v[16];
+              tmem_ld16(taddr + c0, v);
+              tmem_wait_ld(v);
+              if (live) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
-                if (i + 8 * h < a.I) {
-                  *reinterpret_cast<uint4*>(hi + i + 8 * h) =
-                      make_uint4(ph[4 * h], ph[4 * h + 1], ph[4 * h + 2], ph[4 * h + 3]);
-                  *reinterpret_cast<uint4*>(lo + i + 8 * h) =
-                      make_uint4(pl[4 * h], pl[4 * h + 1], pl[4 * h + 2], pl[4 * h + 3]);
+                for (int k = 0; k < 4; ++k)
+                  *reinterpret_cast<float4*>(pb + c0 + 4 * k) =
+                      make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                  __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+              }
+            }
+          }
+          __threadfence();
+          named_bar_sync(1, 128);
+          volatile int* flag = reinterpret_cast<volatile int*>(xchg);
+          const int cf = sk.first_cta(w.tile), cl = sk.last_cta(w.tile);
+          if (threadIdx.x == 64) {
+            const uint32_t done = atomicAdd(&a.cnt[w.tile], 1u);
+            *flag = done == (uint32_t)(cl - cf) ? 1 : 0;
+          }
+          named_bar_sync(1, 128);
+          if (*flag) {
+            __threadfence();
+            if (has && live) {
+              const float wt = __ldg(a.row_w + r);
+              for (int c0 = 0; c0 < kRowsA; c0 += 16) {
+                float g[16], u[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) g[c] = u[c] = 0.0f;
+                for (int c = cf; c <= cl; ++c) {
+                  const float* src =
+                      a.pbuf + (((size_t)c * 2 + sk.part_slot(c, w.tile)) * a.nmax + t) * kWRows;
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    const float4 gv = __ldcg(reinterpret_cast<const float4*>(src + c0) + k);
+                    const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + kRowsA + c0) + k);
+                    g[4 * k] += gv.x; g[4 * k + 1] += gv.y; g[4 * k + 2] += gv.z; g[4 * k + 3] += gv.w;
+                    u[4 * k] += uv.x; u[4 * k + 1] += uv.y; u[4 * k + 2] += uv.z; u[4 * k + 3] += uv.w;
+                  }
                 }
+                swiglu_store16(g, u, wt, hi, lo, w.m0 + c0, a.I);
+              }
             }
+            if (threadIdx.x == 64) a.cnt[w.tile] = 0;  // ready for the next call
           }
         }
       } else {
@@ -870,8 +935,9 @@ struct GroupedPlan {
   int kcA, kcB;      // K chunks (over H, over I)
   int wstA, tstA, tbA;  // gate/up rings: weight depth, token depth, token slot bytes
   int wstB, tstB, tbB;  // down rings
+  int cnt_words;     // gate/up tile counters (>= gate/up tiles)
   size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_re, off_rw, off_xg, off_act, off_y,
-      total;
+      off_pbuf, off_cnt, total;
 };
 
 // Ring depths: token slots (from L2) get up to 48 KB in 2..4 slots, the
@@ -911,7 +977,10 @@ GroupedPlan make_plan(const Problem& p) {
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
   g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
-  g.off_y = o; o += a256(4 * (size_t)kJMax * g.rmax * p.H);
+  g.off_y = o; o += a256(4 * (size_t)kJMaxB * g.rmax * p.H);
+  g.off_pbuf = o; o += a256(4 * (size_t)device_sm_count() * 2 * g.nmaxA * kWRows);
+  g.cnt_words = g.mtA * (p.ep_num + (g.rmax + g.nmaxA - 1) / g.nmaxA);
+  g.off_cnt = o; o += a256(4 * (size_t)g.cnt_words);
   g.total = o;
   return g;
 }
@@ -974,13 +1043,16 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   uint16_t* xg = reinterpret_cast<uint16_t*>(wsb + g.off_xg);
   uint16_t* act = reinterpret_cast<uint16_t*>(wsb + g.off_act);
   float* ypart = reinterpret_cast<float*>(wsb + g.off_y);
+  float* pbuf = reinterpret_cast<float*>(wsb + g.off_pbuf);
+  uint32_t* tcnt = reinterpret_cast<uint32_t*>(wsb + g.off_cnt);
   uint32_t* status = reinterpret_cast<uint32_t*>(ws) + 2;
 
   wr_status_t st = launch_router(p, x, gate_w, nullptr, ids_d, w_d, stream);
   if (st != WR_OK) return st;
   cudaError_t ce = launch_pdl(k_bucket, dim3(1), dim3(512), 0, stream, (const int32_t*)ids_d,
                               (const float*)w_d, p.T * p.K, p.K, p.ep_first, p.ep_num, g.nmaxA,
-                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, re, rw);
+                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, re, rw, tcnt,
+                              g.cnt_words);
   const int gather_blocks = g.rmax < 4 * sms ? g.rmax : 4 * sms;
   if (ce == cudaSuccess)
     ce = launch_pdl(k_gather, dim3(gather_blocks), dim3(256), 0, stream,
@@ -1027,6 +1099,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.row_w = rw;
   ga.act = act;
   ga.ypart = ypart;
+  ga.pbuf = pbuf;
+  ga.cnt = tcnt;
   ga.status = status;
 
   GemmArgs a1 = ga;

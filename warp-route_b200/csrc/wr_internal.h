@@ -59,9 +59,9 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
                          void* ws, cudaStream_t stream, const CommView* comm = nullptr);
 
 // ---- grouped tensor-core path for token batches (wr_grouped.cu) ----
-// Batches of at least this many tokens run as grouped GEMMs over tokens
-// bucketed per expert.
-constexpr int kGroupedMinTokens = 16;
+// Batches of at least this many bf16 tokens run as grouped GEMMs over
+// tokens bucketed per expert (a single token takes the streaming kernel).
+constexpr int kGroupedMinTokens = 2;
 bool grouped_supported(const Problem& p);
 size_t grouped_workspace_bytes(const Problem& p);
 wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w,
