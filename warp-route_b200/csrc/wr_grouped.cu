@@ -59,7 +59,8 @@ constexpr int kWRows = 256;              // MMA N: weight rows per MMA
 constexpr int kRowsA = 128;              // gate/up tile: rows of gate and of up
 constexpr int kRowsB = 256;              // down tile: rows of Wd (= rows of H)
 constexpr int kNMaxA = kTokM;            // tokens per gate/up tile
-constexpr int kNMaxB = 64;               // tokens per down tile (act_hi + act_lo rows <= 128)
+constexpr int kNMaxB = 64;               // tokens per down tile, act_hi and act_lo rows stacked
+constexpr int kNMaxBSplit = 128;         // tokens per down tile, act_hi and act_lo as two A tiles
 constexpr int kRowB = kBK * 2;           // bytes of one row per stage
 constexpr int kWBox = 128;               // weight rows per TMA box
 constexpr int kBoxRows = 16;             // token rows per TMA box
@@ -71,9 +72,13 @@ constexpr int kAccStride = 256;          // columns between accumulator buffers
 constexpr int kSmemMax = 232448;         // 227 KB opt-in shared memory per CTA
 constexpr int kStagePitch = 17;          // down epilogue: floats per parked token (16 + pad)
 constexpr int kXchgBytes = kNMaxB * kStagePitch * 4;
-constexpr int kSmemReserve = 1024 + 512 + kXchgBytes;  // alignment slack, barriers, exchange
+constexpr int kSmemBase = 1024 + 512;    // alignment slack, barriers
+constexpr int kSmemReserve = kSmemBase + kXchgBytes;  // ... and the down epilogue's exchange
 constexpr int kMaxWStages = 8;           // weight ring depth limit
 constexpr int kMaxTStages = 4;           // token ring depth limit
+// barriers (full/empty of both rings, 2 x accumulator full/empty, drain) and
+// three words (TMEM address, abort, fixup flag) in the first 512 bytes
+static_assert((2 * kMaxWStages + 2 * kMaxTStages + 5) * 8 + 12 <= 512, "barrier area");
 constexpr int kJMaxA = 3;                // gate/up: CTAs sharing one tile, at most
 constexpr int kJMaxB = 4;                // down: partial sums per output tile, at most
 
@@ -424,6 +429,7 @@ struct GemmArgs {
   int rmax;            // rows of one activation half (lo rows start at rmax)
   int wstages, tstages;  // weight ring / token ring depth
   int tstage_bytes;      // token slot: gate/up nmax rows, down 2 * nmax rows
+  int hl_split;          // down: act_hi and act_lo are two 128-row A tiles (2 MMAs per step)
   const float* row_w;  // gate/up epilogue: per-row routing weight
   uint16_t* act;       // gate/up output: [2][rmax][I] bf16 (hi, lo)
   float* ypart;        // down output: [kJMaxB][rmax][H] fp32
@@ -587,6 +593,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = tempty + 2;            // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  // down epilogue exchange (stacked act_hi / act_lo only; the host reserves it then)
   float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(fullW) + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -666,8 +674,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int r = 0; r < nbox; ++r)
               tma_load_2d(s + r * kBoxRows * kRowB, &tm_b, kx, w.row0 + r * kBoxRows, &full[st],
                           pol);
-            if (!kGU) {  // act_lo rows at tile rows nmax..
-              uint8_t* sl = s + a.nmax * kRowB;
+            if (!kGU) {  // act_lo rows at tile rows nmax.. (stacked) or in the second A tile
+              uint8_t* sl = s + (a.hl_split ? kTokM : a.nmax) * kRowB;
               for (int r = 0; r < nbox; ++r)
                 tma_load_2d(sl + r * kBoxRows * kRowB, &tm_b, kx, a.rmax + w.row0 + r * kBoxRows,
                             &full[st], pol);
@@ -714,7 +722,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-            umma_bf16(d, sw128_desc(st_addr + kk * 32), sw128_desc(sw_addr + kk * 32), idesc, acc);
+            const uint64_t wdesc = sw128_desc(sw_addr + kk * 32);
+            umma_bf16(d, sw128_desc(st_addr + kk * 32), wdesc, idesc, acc);
+            if (!kGU && a.hl_split)  // act_lo tile into the same accumulator
+              umma_bf16(d, sw128_desc(st_addr + kTokM * kRowB + kk * 32), wdesc, idesc, 1u);
           }
           umma_commit(&emptyW[sw]);
           umma_commit(&emptyT[stt]);
@@ -803,14 +814,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           __threadfence();
           named_bar_sync(1, 128);
-          volatile int* flag = reinterpret_cast<volatile int*>(xchg);
           const int cf = sk.first_cta(w.tile), cl = sk.last_cta(w.tile);
           if (threadIdx.x == 64) {
             const uint32_t done = atomicAdd(&a.cnt[w.tile], 1u);
-            *flag = done == (uint32_t)(cl - cf) ? 1 : 0;
+            *last_flag = done == (uint32_t)(cl - cf) ? 1 : 0;
           }
           named_bar_sync(1, 128);
-          if (*flag) {
+          if (*last_flag) {
             __threadfence();
             if (has && live) {
               const float wt = __ldg(a.row_w + r);
@@ -836,39 +846,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       } else {
-        // lanes 0..nmax-1: act_hi part of the tile's tokens, lanes nmax..:
-        // act_lo part.  Threads holding a lo part park it in smem; the
-        // thread holding the hi part of the same token adds and stores 16
-        // consecutive outputs.
-        const int L = 32 * q + lane;                  // accumulator lane
-        const bool lo_lane = L >= a.nmax && L < a.nmax + w.n;
-        const bool hi_lane = L < w.n;
-        const bool has = 32 * q < a.nmax + w.n;      // warp-uniform: some lane is used
-        float* park = xchg + (lo_lane ? L - a.nmax : (hi_lane ? L : 0)) * kStagePitch;
-        float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + L) * a.H;
-        for (int c0 = 0; c0 < kWRows; c0 += 16) {
-          uint32_t v[16];
-          if (has) {
-            tmem_ld16(taddr + c0, v);
-            tmem_wait_ld(v);
-            if (lo_lane) {
+        if (a.hl_split) {
+          // lane t holds token t's whole output (act_hi and act_lo summed by
+          // the MMAs): store 16 consecutive outputs per step.
+          const int t = 32 * q + lane;
+          if (32 * q < w.n) {  // warp-uniform
+            float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + t) * a.H;
+            for (int c0 = 0; c0 < kWRows; c0 += 16) {
+              uint32_t v[16];
+              tmem_ld16(taddr + c0, v);
+              tmem_wait_ld(v);
+              const int h = w.m0 + c0;
+              if (t < w.n) {
 #pragma unroll
-              for (int c = 0; c < 16; ++c) park[c] = __uint_as_float(v[c]);
+                for (int k = 0; k < 4; ++k)
+                  if (h + 4 * k < a.H)
+                    *reinterpret_cast<float4*>(yrow + h + 4 * k) =
+                        make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                    __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+              }
             }
           }
-          named_bar_sync(1, 128);
-          if (hi_lane) {
-            const int h = w.m0 + c0;
+        } else {
+          // lanes 0..nmax-1: act_hi part of the tile's tokens, lanes nmax..:
+          // act_lo part.  Threads holding a lo part park it in smem; the
+          // thread holding the hi part of the same token adds and stores 16
+          // consecutive outputs.
+          const int L = 32 * q + lane;                  // accumulator lane
+          const bool lo_lane = L >= a.nmax && L < a.nmax + w.n;
+          const bool hi_lane = L < w.n;
+          const bool has = 32 * q < a.nmax + w.n;      // warp-uniform: some lane is used
+          float* park = xchg + (lo_lane ? L - a.nmax : (hi_lane ? L : 0)) * kStagePitch;
+          float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + L) * a.H;
+          for (int c0 = 0; c0 < kWRows; c0 += 16) {
+            uint32_t v[16];
+            if (has) {
+              tmem_ld16(taddr + c0, v);
+              tmem_wait_ld(v);
+              if (lo_lane) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (h + 4 * k < a.H)
-                *reinterpret_cast<float4*>(yrow + h + 4 * k) =
-                    make_float4(__uint_as_float(v[4 * k]) + park[4 * k],
-                                __uint_as_float(v[4 * k + 1]) + park[4 * k + 1],
-                                __uint_as_float(v[4 * k + 2]) + park[4 * k + 2],
-                                __uint_as_float(v[4 * k + 3]) + park[4 * k + 3]);
+                for (int c = 0; c < 16; ++c) park[c] = __uint_as_float(v[c]);
+              }
+            }
+            named_bar_sync(1, 128);
+            if (hi_lane) {
+              const int h = w.m0 + c0;
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                if (h + 4 * k < a.H)
+                  *reinterpret_cast<float4*>(yrow + h + 4 * k) =
+                      make_float4(__uint_as_float(v[4 * k]) + park[4 * k],
+                                  __uint_as_float(v[4 * k + 1]) + park[4 * k + 1],
+                                  __uint_as_float(v[4 * k + 2]) + park[4 * k + 2],
+                                  __uint_as_float(v[4 * k + 3]) + park[4 * k + 3]);
+            }
+            named_bar_sync(1, 128);
           }
-          named_bar_sync(1, 128);
         }
       }
       tc_fence_before();
@@ -935,17 +968,28 @@ struct GroupedPlan {
   int kcA, kcB;      // K chunks (over H, over I)
   int wstA, tstA, tbA;  // gate/up rings: weight depth, token depth, token slot bytes
   int wstB, tstB, tbB;  // down rings
+  int hl_split;         // down: act_hi / act_lo as two 128-row A tiles
   int cnt_words;     // gate/up tile counters (>= gate/up tiles)
   size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_re, off_rw, off_xg, off_act, off_y,
       off_pbuf, off_cnt, total;
 };
 
-// Ring depths: token slots (from L2) get up to 48 KB in 2..4 slots, the
-// weights (from HBM) every remaining byte, up to kMaxWStages.
-void ring_split(int tbytes, int* wst, int* tst) {
-  int t = 49152 / tbytes;
-  t = t < 2 ? 2 : (t > kMaxTStages ? kMaxTStages : t);
-  int w = (kSmemMax - kSmemReserve - t * tbytes) / kWStageBytes;
+// Ring depths.  Weights come from HBM and want >= 5 stages of 32 KB in
+// flight; token tiles come from L2, but a slot is held until its MMAs finish,
+// so 2 slots leave the MMA waiting on L2 latency.  Take the most token slots
+// (<= 4) that still leave 5 weight stages; large token slots (>= 32 KB) may
+// drop to 4 weight stages for a third slot.
+void ring_split(int tbytes, int reserve, int* wst, int* tst) {
+  const int avail = kSmemMax - reserve;
+  int t = kMaxTStages, w = 0;
+  for (; t >= 2; --t) {
+    w = (avail - t * tbytes) / kWStageBytes;
+    if (w >= 5 || (tbytes >= 32768 && t >= 3 && w >= 4)) break;
+  }
+  if (t < 2) {
+    t = 2;
+    w = (avail - t * tbytes) / kWStageBytes;
+  }
   // the last token slot's 128-row MMA window must end inside the allocation
   static_assert(kTokBytes <= 4 * kWStageBytes, "token window overhang");
   *tst = t;
@@ -957,16 +1001,17 @@ GroupedPlan make_plan(const Problem& p) {
   const int TK = p.T * p.K;
   const int n16 = (p.T + 15) & ~15;
   g.nmaxA = n16 < kNMaxA ? n16 : kNMaxA;
-  g.nmaxB = n16 < kNMaxB ? n16 : kNMaxB;
+  g.hl_split = n16 > kNMaxB;
+  g.nmaxB = g.hl_split ? kNMaxBSplit : n16;
   g.rmax = (TK + 15 * p.ep_num + 15) & ~15;
   g.mtA = (p.I + kRowsA - 1) / kRowsA;
   g.mtB = (p.H + kRowsB - 1) / kRowsB;
   g.kcA = (p.H + kBK - 1) / kBK;
   g.kcB = (p.I + kBK - 1) / kBK;
   g.tbA = g.nmaxA * kRowB;
-  g.tbB = 2 * g.nmaxB * kRowB;
-  ring_split(g.tbA, &g.wstA, &g.tstA);
-  ring_split(g.tbB, &g.wstB, &g.tstB);
+  g.tbB = g.hl_split ? 2 * kTokM * kRowB : 2 * g.nmaxB * kRowB;
+  ring_split(g.tbA, kSmemBase, &g.wstA, &g.tstA);
+  ring_split(g.tbB, g.hl_split ? kSmemBase : kSmemReserve, &g.wstB, &g.tstB);
   size_t o = kWsControlBytes;
   g.off_ids = o; o += a256(4 * (size_t)TK);
   g.off_w = o; o += a256(4 * (size_t)TK);
@@ -1103,13 +1148,14 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.cnt = tcnt;
   ga.status = status;
 
+  ga.hl_split = 0;
   GemmArgs a1 = ga;
   a1.nmax = g.nmaxA;
   a1.kc_total = g.kcA;
   a1.wstages = g.wstA;
   a1.tstages = g.tstA;
   a1.tstage_bytes = g.tbA;
-  const size_t smemA = (size_t)g.wstA * kWStageBytes + (size_t)g.tstA * g.tbA + kSmemReserve;
+  const size_t smemA = (size_t)g.wstA * kWStageBytes + (size_t)g.tstA * g.tbA + kSmemBase;
   ce = launch_pdl(k_grouped_gemm<true>, dim3(sms), dim3(kGemmThreads), smemA, stream, tm_gu,
                   tm_x, a1);
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (gate/up) launch");
@@ -1120,7 +1166,9 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   a2.wstages = g.wstB;
   a2.tstages = g.tstB;
   a2.tstage_bytes = g.tbB;
-  const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB + kSmemReserve;
+  a2.hl_split = g.hl_split;
+  const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB +
+                       (g.hl_split ? kSmemBase : kSmemReserve);
   ce = launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream, tm_dn,
                   tm_act, a2);
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (down) launch");
