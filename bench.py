@@ -73,6 +73,8 @@ def parse():
                     help="batched-decode sweep token counts (N = 1 only); empty: no sweep")
     ap.add_argument("--sweep-layers", type=int, default=32)
     ap.add_argument("--sweep-steps", type=int, default=3)
+    ap.add_argument("--only-sweep", action="store_true",
+                    help="run only the batched-decode sweep (N = 1) and print its JSON line")
     return ap.parse_args()
 
 
@@ -585,6 +587,13 @@ def main():
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference_arm(args, world, rank)
+        return
+    if args.only_sweep:
+        if world != 1:
+            raise SystemExit("--only-sweep runs on one GPU")
+        torch.cuda.set_device(local)
+        sweep = batched_sweep(args, torch.device("cuda", local))
+        print(json.dumps({"batched_sweep": sweep}), flush=True)
         return
     run_ours(args, world, rank, local)
 
