@@ -20,12 +20,14 @@ measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
 composition (restated in oracle/torch_composition.py) on a bounded sample.
 `--impl reference` times that CPU composition alone, as the reference arm.
 
-At N = 1 the line also carries `batched_sweep`: the batched-decode sweep on
+The line also carries `batched_sweep`: the batched-decode sweep on
 the Mixtral shape (tokens 1, 4, 16, 64, 256; router bias N(0,1) per expert to
 skew the load; 32 stacked layers with independent weights, each applied to
 the same seeded token batch), µs per layer from CUDA-graph replays of the 32
 layer calls.  Batches of two or more bf16 tokens run on the grouped
-tensor-core path (tcgen05 GEMMs over tokens bucketed per expert).
+tensor-core path (tcgen05 GEMMs over tokens bucketed per expert).  At N > 1
+the sweep is expert parallel (E/N experts of every layer per GPU) with one
+NCCL all-reduce of the layer output, both inside the replayed graph.
 """
 from __future__ import annotations
 
@@ -40,6 +42,8 @@ import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
+# NCCL's version banner would land on stdout ahead of the one JSON line
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 sys.path.insert(0, os.path.join(REPO, "warp-route_b200"))
 
 import torch  # noqa: E402
@@ -70,7 +74,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=0,
                     help="rotating layers (0: enough to exceed 4x L2 between reuses)")
     ap.add_argument("--sweep-tokens", default="1,4,16,64,256",
-                    help="batched-decode sweep token counts (N = 1 only); empty: no sweep")
+                    help="batched-decode sweep token counts; empty: no sweep")
     ap.add_argument("--sweep-layers", type=int, default=32)
     ap.add_argument("--sweep-steps", type=int, default=3)
     ap.add_argument("--only-sweep", action="store_true",
@@ -243,10 +247,15 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def batched_sweep(args, dev):
+def batched_sweep(args, dev, world=1, rank=0):
     """The batched-decode sweep (Mixtral shape, router bias, stacked layers):
     per token count, µs per layer over CUDA-graph replays of one step (every
-    layer once) and the HBM GB/s of the distinct experts each layer streams."""
+    layer once) and the HBM GB/s of the distinct experts each layer streams.
+    N > 1: expert parallel (rank r holds experts [r E/N, (r+1) E/N) of every
+    layer) and one NCCL all-reduce of the [T, H] output per layer, inside the
+    graph; the time is the max over ranks."""
+    import torch.distributed as dist
+
     from warp_route import functional as F
     from warp_route import synthetic
 
@@ -254,9 +263,12 @@ def batched_sweep(args, dev):
     if not tokens:
         return None
     E, H, I, K = SHAPES["mixtral"]
+    if E % world:
+        return None
     nl = args.sweep_layers
     layers = [synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, device=dev, seed=900 + li,
-                                   layer=li, router_bias=True) for li in range(nl)]
+                                   layer=li, router_bias=True, ep_rank=rank, ep_size=world)
+              for li in range(nl)]
     results = []
     stream = torch.cuda.Stream()
     for T in tokens:
@@ -264,20 +276,25 @@ def batched_sweep(args, dev):
         gx.manual_seed(7000 + T)
         x = torch.randn(T, H, generator=gx, device=dev).to(torch.bfloat16)
         xin = x[0].contiguous() if T == 1 else x
-        distinct = []
+        distinct, local_max = [], []
         for Lr in layers:
             _, ids, _ = F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
-                                           router_bias=Lr.router_bias)
-            distinct.append(len(set(ids.cpu().view(-1).tolist())))
+                                           router_bias=Lr.router_bias,
+                                           ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)
+            sel = set(ids.cpu().view(-1).tolist())
+            distinct.append(len(sel))
+            if world > 1:
+                local_max.append(max(sum(1 for e in sel if r * (E // world) <= e < (r + 1) * (E // world))
+                                     for r in range(world)))
 
         def step():
             for Lr in layers:
-                if T == 1:
-                    F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
-                                       router_bias=Lr.router_bias)
-                else:
-                    F.batched_fused_moe(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
-                                        router_bias=Lr.router_bias)
+                out = F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
+                                         router_bias=Lr.router_bias,
+                                         ep_first_expert=Lr.ep_first,
+                                         ep_num_local=Lr.ep_num)[0]
+                if world > 1:
+                    dist.all_reduce(out)
 
         with torch.cuda.stream(stream):
             for _ in range(2):
@@ -289,6 +306,8 @@ def batched_sweep(args, dev):
         for _ in range(2):
             g.replay()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(dev.index) as clk:
             t0.record(stream)
@@ -297,26 +316,36 @@ def batched_sweep(args, dev):
                     g.replay()
             t1.record(stream)
             torch.cuda.synchronize()
-        us = t0.elapsed_time(t1) * 1000.0 / (args.sweep_steps * nl)
+        tt = torch.tensor([t0.elapsed_time(t1)], device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        us = tt.item() * 1000.0 / (args.sweep_steps * nl)
         with torch.cuda.stream(stream):
             st = F._load_extension().workspace_status(xin)
         if st != 0:
             raise SystemExit(f"batched sweep T={T}: device status {st}: timing discarded")
         del g
+        torch.cuda.synchronize()
         mean_distinct = sum(distinct) / len(distinct)
         wbytes = mean_distinct * 3 * H * I * 2
-        results.append({"tokens": T, "us_per_layer": round(us, 2),
-                        "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
-                        "experts_per_layer": round(mean_distinct, 2),
-                        "path": "streaming kernel" if T == 1 else "grouped tcgen05 GEMMs",
-                        "clocks": clk.summary()})
+        r = {"tokens": T, "us_per_layer": round(us, 2),
+             "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+             "experts_per_layer": round(mean_distinct, 2),
+             "path": "streaming kernel" if T == 1 else "grouped tcgen05 GEMMs",
+             "clocks": clk.summary()}
+        if world > 1:
+            r["busiest_rank_experts"] = round(sum(local_max) / len(local_max), 2)
+            r["hbm_gbs_note"] = "aggregate over all ranks"
+        results.append(r)
     del layers
     torch.cuda.empty_cache()
+    par = f"expert parallel over {world} GPUs ({E // world} experts each), NCCL all-reduce " \
+          f"of the [T,H] fp32 output in the graph" if world > 1 else "single GPU"
     return {"config": "mixtral, router bias N(0,1), bf16", "layers": nl,
-            "steps": args.sweep_steps,
+            "steps": args.sweep_steps, "parallelism": par,
             "note": "each layer has its own weights, gate and bias and takes the same seeded "
-                    "token batch; value = µs per layer (graph replays of the layer stack); "
-                    "hbm_gbs = distinct selected experts' weight bytes / time",
+                    "token batch; value = µs per layer (graph replays of the layer stack, max "
+                    "over ranks); hbm_gbs = distinct selected experts' weight bytes / time",
             "results": results}
 
 
@@ -530,9 +559,7 @@ def run_ours(args, world, rank, local):
                          f"selected experts widened to fp32, median of {ncalls} after 3 warm-ups; "
                          f"warp-route's torch composition restated in oracle/torch_composition.py"}
 
-    sweep = None
-    if world == 1 and rank == 0:
-        sweep = batched_sweep(args, dev)
+    sweep = batched_sweep(args, dev, world, rank)
 
     if world > 1:
         dist.barrier()
