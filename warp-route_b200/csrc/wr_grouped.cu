@@ -79,6 +79,7 @@ constexpr int kMaxTStages = 4;           // token ring depth limit
 // barriers (full/empty of both rings, 2 x accumulator full/empty, drain) and
 // three words (TMEM address, abort, fixup flag) in the first 512 bytes
 static_assert((2 * kMaxWStages + 2 * kMaxTStages + 5) * 8 + 12 <= 512, "barrier area");
+constexpr int kBucketSmemIds = 5632;    // k_bucket stages up to this many ids + weights (44 KB)
 constexpr int kJMaxA = 3;                // gate/up: CTAs sharing one tile, at most
 constexpr int kJMaxB = 4;                // down: partial sums per output tile, at most
 
@@ -238,7 +239,9 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 // One CTA.  Pairs (t, k) whose expert is in [ep_first, ep_first + E) get a
 // row: expert e's rows are base[e] .. base[e] + cnt[e] - 1 in ascending
 // token order, followed by zero-weight padding up to a multiple of 16.
-// Pairs of other ranks' experts get slot -1.  Zeroes the gate/up tile
+// Pairs of other ranks' experts get slot -1.  Each row also gets its first
+// down tile and the tile stride between H tiles (row_tile), which the
+// combine uses.  Zeroes the gate/up tile
 // counters (robust against a call that gave up half-way).  Also writes the tile counts
 // the GEMM kernels walk: per expert ntlA (ntlB) token tiles of <= nmaxA
 // (nmaxB) rows, mtA * ntlA gate/up tiles and mtB * ntlB down tiles.
@@ -248,23 +251,36 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
                                                 int mtA, int mtB, int* __restrict__ meta,
                                                 int32_t* __restrict__ slot,
                                                 int32_t* __restrict__ row_tok,
-                                                int32_t* __restrict__ row_e,
+                                                int2* __restrict__ row_tile,
                                                 float* __restrict__ row_w,
                                                 uint32_t* __restrict__ tile_cnt, int cnt_words) {
+  extern __shared__ int s_ids[];  // ids, then weights, staged here when TK <= kBucketSmemIds
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_base[kMaxExperts];
+  __shared__ int s_preB[kMaxExperts];
+  __shared__ int s_ntlB[kMaxExperts];
   griddep_wait();
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const bool staged = TK <= kBucketSmemIds;
   for (int i = threadIdx.x; i < cnt_words; i += blockDim.x) tile_cnt[i] = 0u;
+  float* s_w = reinterpret_cast<float*>(s_ids + TK);
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
-    const int e = ids[i] - ep_first;
+    const int id = ids[i];
+    if (staged) {
+      s_ids[i] = id;
+      s_w[i] = w[i];
+    }
+    const int e = id - ep_first;
     if (e < 0 || e >= E) slot[i] = -1;
   }
+  __syncthreads();
+  const int* sid = staged ? s_ids : ids;
+  const float* sw = staged ? s_w : w;
   for (int e = warp; e < E; e += nw) {
     int c = 0;
     for (int j = 0; j < TK; j += 32) {
-      const bool m = j + lane < TK && ids[j + lane] == e + ep_first;
+      const bool m = j + lane < TK && sid[j + lane] == e + ep_first;
       c += __popc(__ballot_sync(0xffffffffu, m));
     }
     if (lane == 0) s_cnt[e] = c;
@@ -288,8 +304,10 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
       s_base[e] = b;
       ntlA[e] = na;
       ntlB[e] = nb;
+      s_ntlB[e] = nb;
       preA[e] = pa;
       preB[e] = pb;
+      s_preB[e] = pb;
       b += np;
       pa += mtA * na;
       pb += mtB * nb;
@@ -302,23 +320,24 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
   }
   __syncthreads();
   for (int e = warp; e < E; e += nw) {
-    int run = s_base[e];
+    const int b0 = s_base[e];
+    int run = b0;
     for (int j = 0; j < TK; j += 32) {
-      const bool m = j + lane < TK && ids[j + lane] == e + ep_first;
+      const bool m = j + lane < TK && sid[j + lane] == e + ep_first;
       const unsigned bal = __ballot_sync(0xffffffffu, m);
       if (m) {
         const int r = run + __popc(bal & ((1u << lane) - 1u));
         slot[j + lane] = r;
         row_tok[r] = (j + lane) / K;
-        row_e[r] = e;
-        row_w[r] = w[j + lane];
+        row_tile[r] = make_int2(s_preB[e] + (r - b0) / nmaxB, s_ntlB[e]);
+        row_w[r] = sw[j + lane];
       }
       run += __popc(bal);
     }
-    const int end = s_base[e] + ((s_cnt[e] + 15) & ~15);
+    const int end = b0 + ((s_cnt[e] + 15) & ~15);
     for (int r = run + lane; r < end; r += 32) {
       row_tok[r] = -1;
-      row_e[r] = e;
+      row_tile[r] = make_int2(s_preB[e] + (r - b0) / nmaxB, s_ntlB[e]);
       row_w[r] = 0.0f;
     }
   }
@@ -384,27 +403,25 @@ WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid, int jmax) {
 // partials in slot order : 0).  One fixed order: deterministic.
 __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypart,
                                                  const int32_t* __restrict__ slot,
-                                                 const int32_t* __restrict__ row_e,
-                                                 const int* __restrict__ meta, int E, int K,
-                                                 int H4, int rmax, int kcB, int nmaxB, int grid,
+                                                 const int2* __restrict__ row_tile,
+                                                 const int* __restrict__ meta, int K, int H4,
+                                                 int rmax, int kcB, int grid,
                                                  float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
-  const MetaView mv = meta_view(meta, E);
   const SplitK sk = make_splitk(meta[2], kcB, grid, kJMaxB);
   const int mt = (h * 4) / kRowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
     const int r = slot[(int64_t)t * K + k];
     if (r < 0) continue;
-    const int e = row_e[r];
-    const int nt = (r - mv.base[e]) / nmaxB;
-    const int64_t tile = (int64_t)mv.preB[e] + (int64_t)mt * mv.ntlB[e] + nt;
-    const int c0 = sk.first_cta((int)tile);
-    const int c1 = sk.last_cta((int)tile);
+    const int2 rt = row_tile[r];
+    const int tile = rt.x + mt * rt.y;
+    const int c0 = sk.first_cta(tile);
+    const int c1 = sk.last_cta(tile);
     for (int j = 0; j <= c1 - c0; ++j) {
       const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h];
       acc.x += v.x;
@@ -1018,7 +1035,7 @@ GroupedPlan make_plan(const Problem& p) {
   g.off_slot = o; o += a256(4 * (size_t)TK);
   g.off_meta = o; o += a256(4 * (size_t)meta_words(p.ep_num));
   g.off_rtok = o; o += a256(4 * (size_t)g.rmax);
-  g.off_re = o; o += a256(4 * (size_t)g.rmax);
+  g.off_re = o; o += a256(8 * (size_t)g.rmax);
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
   g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
@@ -1083,7 +1100,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   int32_t* slot = reinterpret_cast<int32_t*>(wsb + g.off_slot);
   int* meta = reinterpret_cast<int*>(wsb + g.off_meta);
   int32_t* rtok = reinterpret_cast<int32_t*>(wsb + g.off_rtok);
-  int32_t* re = reinterpret_cast<int32_t*>(wsb + g.off_re);
+  int2* rtile = reinterpret_cast<int2*>(wsb + g.off_re);
   float* rw = reinterpret_cast<float*>(wsb + g.off_rw);
   uint16_t* xg = reinterpret_cast<uint16_t*>(wsb + g.off_xg);
   uint16_t* act = reinterpret_cast<uint16_t*>(wsb + g.off_act);
@@ -1094,9 +1111,12 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
 
   wr_status_t st = launch_router(p, x, gate_w, nullptr, ids_d, w_d, stream);
   if (st != WR_OK) return st;
-  cudaError_t ce = launch_pdl(k_bucket, dim3(1), dim3(512), 0, stream, (const int32_t*)ids_d,
+  const int TK = p.T * p.K;
+  const size_t bucket_smem = TK <= kBucketSmemIds ? 8 * (size_t)TK : 0;
+  cudaError_t ce = launch_pdl(k_bucket, dim3(1), dim3(512), bucket_smem, stream,
+                              (const int32_t*)ids_d,
                               (const float*)w_d, p.T * p.K, p.K, p.ep_first, p.ep_num, g.nmaxA,
-                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, re, rw, tcnt,
+                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, rtile, rw, tcnt,
                               g.cnt_words);
   const int gather_blocks = g.rmax < 4 * sms ? g.rmax : 4 * sms;
   if (ce == cudaSuccess)
@@ -1176,8 +1196,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   const int H4 = p.H / 4;
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                  (const int32_t*)re, (const int*)meta, p.ep_num, p.K, H4, g.rmax, g.kcB,
-                  g.nmaxB, sms, reinterpret_cast<float4*>(out));
+                  (const int2*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms,
+                  reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 

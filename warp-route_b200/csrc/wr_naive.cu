@@ -21,11 +21,10 @@ namespace wr {
 namespace {
 
 constexpr int kRouterThreads = 32 * kRouterSegments;
-// k_router's static shared memory (segment partials, logits, ids, weights).
-constexpr int kRouterStaticSmem = 4 * (kRouterSegments * kMaxExperts + 3 * kMaxExperts);
 
-// One CTA per token: x -> shared memory (fp32), logits by warps, softmax +
-// top-K by thread 0.
+// One CTA per token: warp j computes segment j of every router row, reading
+// x straight from global memory in 16-byte vectors (no staging: the loads of
+// all rows and x are in flight together); softmax + top-K by warp 0.
 template <typename Tw>
 __global__ void __launch_bounds__(kRouterThreads) k_router(const Tw* __restrict__ x,
                                                            const Tw* __restrict__ gate_w,
@@ -34,18 +33,16 @@ __global__ void __launch_bounds__(kRouterThreads) k_router(const Tw* __restrict_
                                                            float* __restrict__ logits_out,
                                                            int32_t* __restrict__ ids_out,
                                                            float* __restrict__ w_out) {
-  extern __shared__ __align__(16) float xs[];
   __shared__ float parts[kRouterSegments * kMaxExperts];
   __shared__ float lg[kMaxExperts];
   __shared__ int ids[kMaxExperts];
   __shared__ float ws[kMaxExperts];
   const int t = blockIdx.x;
   const Tw* xt = x + (int64_t)t * H;
-  for (int h = threadIdx.x; h < H; h += blockDim.x) xs[h] = load_scalar<Tw>(xt, h);
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // blockDim.x == 32 * kRouterSegments: warp j computes segment j of every row.
-  router_segment_warp<Tw>(gate_w, XSmem{xs}, E, H, warp, lane, vec_ok, parts + warp * kMaxExperts);
+  router_segment_warp<Tw>(gate_w, XGlobal<Tw>{xt}, E, H, warp, lane, vec_ok,
+                          parts + warp * kMaxExperts);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     lg[e] = router_combine(parts, kMaxExperts, e, bias);
@@ -112,21 +109,10 @@ __global__ void k_weighted_accum(float* __restrict__ out, const float* __restric
 template <typename Tw>
 wr_status_t router_impl(const Problem& p, const void* x, const void* gate_w, float* logits,
                         int32_t* ids, float* w, cudaStream_t stream) {
-  const size_t smem = (size_t)p.H * sizeof(float);
-  static std::once_flag once[64];
-  static cudaError_t err[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::call_once(once[dev & 63], [&] {
-    err[dev & 63] = cudaFuncSetAttribute(k_router<Tw>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         232448 - kRouterStaticSmem);
-  });
-  if (err[dev & 63] != cudaSuccess) return cuda_fail(err[dev & 63], "cudaFuncSetAttribute(router)");
-  if (smem > (size_t)(232448 - kRouterStaticSmem))
-    return fail(WR_ERR_UNSUPPORTED, "hidden_dim %d too large for the router kernel", p.H);
   const int vec = 16 / p.elt;
-  const bool vec_ok = (p.H % vec == 0) && ((reinterpret_cast<uintptr_t>(gate_w) & 15) == 0);
-  k_router<Tw><<<p.T, kRouterThreads, smem, stream>>>(
+  const bool vec_ok = (p.H % vec == 0) && ((reinterpret_cast<uintptr_t>(gate_w) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  k_router<Tw><<<p.T, kRouterThreads, 0, stream>>>(
       static_cast<const Tw*>(x), static_cast<const Tw*>(gate_w), p.router_bias, p.E, p.H, p.K,
       vec_ok, logits, ids, w);
   cudaError_t e = cudaGetLastError();
