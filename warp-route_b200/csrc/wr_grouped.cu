@@ -81,7 +81,8 @@ constexpr int kMaxTStages = 4;           // token ring depth limit
 static_assert((2 * kMaxWStages + 2 * kMaxTStages + 5) * 8 + 12 <= 512, "barrier area");
 constexpr int kBucketSmemIds = 5632;    // k_bucket stages up to this many ids + weights (44 KB)
 constexpr int kJMaxA = 3;                // gate/up: CTAs sharing one tile, at most
-constexpr int kJMaxB = 4;                // down: partial sums per output tile, at most
+constexpr int kJMaxB = 4;                // down: partial sums per output tile, at least this cap
+constexpr int kJMaxBLimit = 16;          // ... and at most this one (few tiles: expert parallel)
 
 // Bucket metadata (int32 words in the workspace), written by k_bucket:
 //   [0] rows in use, [1] gate/up tiles, [2] down tiles, and from word 16
@@ -405,14 +406,14 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
                                                  const int32_t* __restrict__ slot,
                                                  const int2* __restrict__ row_tile,
                                                  const int* __restrict__ meta, int K, int H4,
-                                                 int rmax, int kcB, int grid,
+                                                 int rmax, int kcB, int grid, int jmax,
                                                  float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
-  const SplitK sk = make_splitk(meta[2], kcB, grid, kJMaxB);
+  const SplitK sk = make_splitk(meta[2], kcB, grid, jmax);
   const int mt = (h * 4) / kRowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
@@ -449,7 +450,8 @@ struct GemmArgs {
   int hl_split;          // down: act_hi and act_lo are two 128-row A tiles (2 MMAs per step)
   const float* row_w;  // gate/up epilogue: per-row routing weight
   uint16_t* act;       // gate/up output: [2][rmax][I] bf16 (hi, lo)
-  float* ypart;        // down output: [kJMaxB][rmax][H] fp32
+  float* ypart;        // down output: [jmax][rmax][H] fp32
+  int jmax;            // CTAs per tile, at most (gate/up: kJMaxA)
   float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32
   uint32_t* cnt;       // gate/up: CTAs done with each cut tile (zeroed by k_bucket)
   uint32_t* status;
@@ -487,7 +489,7 @@ struct WorkIter {
   WR_DEVINL bool init(const GemmArgs& a) {
     e = 0;
     sk = make_splitk(__ldg(a.meta + (kGU ? 1 : 2)), a.kc_total, gridDim.x,
-                     kGU ? kJMaxA : kJMaxB);
+                     a.jmax);
     if (sk.U == 0 || (int)blockIdx.x >= sk.G) return false;
     u = sk.u_lo(blockIdx.x);
     u1 = sk.u_lo(blockIdx.x + 1);
@@ -839,25 +841,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           named_bar_sync(1, 128);
           if (*last_flag) {
             __threadfence();
-            if (has && live) {
-              const float wt = __ldg(a.row_w + r);
-              for (int c0 = 0; c0 < kRowsA; c0 += 16) {
-                float g[16], u[16];
+            // The partials live in global memory, so all 128 epilogue threads
+            // share the work: item = (token, 16 intermediate rows).
+            const int et = threadIdx.x - 64;
+            for (int item = et; item < w.n * (kRowsA / 16); item += 128) {
+              const int tt = item / (kRowsA / 16);
+              const int c0 = (item % (kRowsA / 16)) * 16;
+              const int rr = w.row0 + tt;
+              float g[16], u[16];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) g[c] = u[c] = 0.0f;
-                for (int c = cf; c <= cl; ++c) {
-                  const float* src =
-                      a.pbuf + (((size_t)c * 2 + sk.part_slot(c, w.tile)) * a.nmax + t) * kWRows;
+              for (int c = 0; c < 16; ++c) g[c] = u[c] = 0.0f;
+              for (int c = cf; c <= cl; ++c) {
+                const float* src =
+                    a.pbuf + (((size_t)c * 2 + sk.part_slot(c, w.tile)) * a.nmax + tt) * kWRows;
 #pragma unroll
-                  for (int k = 0; k < 4; ++k) {
-                    const float4 gv = __ldcg(reinterpret_cast<const float4*>(src + c0) + k);
-                    const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + kRowsA + c0) + k);
-                    g[4 * k] += gv.x; g[4 * k + 1] += gv.y; g[4 * k + 2] += gv.z; g[4 * k + 3] += gv.w;
-                    u[4 * k] += uv.x; u[4 * k + 1] += uv.y; u[4 * k + 2] += uv.z; u[4 * k + 3] += uv.w;
-                  }
+                for (int k = 0; k < 4; ++k) {
+                  const float4 gv = __ldcg(reinterpret_cast<const float4*>(src + c0) + k);
+                  const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + kRowsA + c0) + k);
+                  g[4 * k] += gv.x; g[4 * k + 1] += gv.y; g[4 * k + 2] += gv.z; g[4 * k + 3] += gv.w;
+                  u[4 * k] += uv.x; u[4 * k + 1] += uv.y; u[4 * k + 2] += uv.z; u[4 * k + 3] += uv.w;
                 }
-                swiglu_store16(g, u, wt, hi, lo, w.m0 + c0, a.I);
               }
+              uint16_t* hrow = a.act + (int64_t)rr * a.I;
+              swiglu_store16(g, u, __ldg(a.row_w + rr), hrow, hrow + (int64_t)a.rmax * a.I,
+                             w.m0 + c0, a.I);
             }
             if (threadIdx.x == 64) a.cnt[w.tile] = 0;  // ready for the next call
           }
@@ -987,6 +994,7 @@ struct GroupedPlan {
   int wstB, tstB, tbB;  // down rings
   int hl_split;         // down: act_hi / act_lo as two 128-row A tiles
   int cnt_words;     // gate/up tile counters (>= gate/up tiles)
+  int jmaxB;         // down: partial sums per tile, at most
   size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_re, off_rw, off_xg, off_act, off_y,
       off_pbuf, off_cnt, total;
 };
@@ -1039,7 +1047,12 @@ GroupedPlan make_plan(const Problem& p) {
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
   g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
-  g.off_y = o; o += a256(4 * (size_t)kJMaxB * g.rmax * p.H);
+  // Down partials per tile: enough that the fewest possible tiles (one active
+  // expert) still spread over every SM.
+  g.jmaxB = (device_sm_count() + g.mtB - 1) / g.mtB + 1;
+  if (g.jmaxB < kJMaxB) g.jmaxB = kJMaxB;
+  if (g.jmaxB > kJMaxBLimit) g.jmaxB = kJMaxBLimit;
+  g.off_y = o; o += a256(4 * (size_t)g.jmaxB * g.rmax * p.H);
   g.off_pbuf = o; o += a256(4 * (size_t)device_sm_count() * 2 * g.nmaxA * kWRows);
   g.cnt_words = g.mtA * (p.ep_num + (g.rmax + g.nmaxA - 1) / g.nmaxA);
   g.off_cnt = o; o += a256(4 * (size_t)g.cnt_words);
@@ -1172,6 +1185,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   GemmArgs a1 = ga;
   a1.nmax = g.nmaxA;
   a1.kc_total = g.kcA;
+  a1.jmax = kJMaxA;
   a1.wstages = g.wstA;
   a1.tstages = g.tstA;
   a1.tstage_bytes = g.tbA;
@@ -1183,6 +1197,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   GemmArgs a2 = ga;
   a2.nmax = g.nmaxB;
   a2.kc_total = g.kcB;
+  a2.jmax = g.jmaxB;
   a2.wstages = g.wstB;
   a2.tstages = g.tstB;
   a2.tstage_bytes = g.tbB;
@@ -1196,7 +1211,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   const int H4 = p.H / 4;
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                  (const int2*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms,
+                  (const int2*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
                   reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
