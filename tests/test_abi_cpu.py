@@ -127,6 +127,24 @@ def test_workspace_sizes_cover_activations():
     assert lib.wr_naive_moe_workspace_size(ctypes.byref(d)) >= 3 * 14336 * 4
 
 
+def test_grouped_workspace_covers_its_buffers():
+    """Batches of >= 2 bf16 tokens take the grouped path, whose workspace holds
+    the bucketed tokens, the hi/lo activations and the down partial sums."""
+    lib = _abi.load()
+    E, H, I, K, T = 8, 4096, 14336, 2, 256
+    d = _abi.desc(E, H, I, K, _abi.WR_DTYPE_BF16)
+    need = lib.wr_fused_moe_workspace_size(ctypes.byref(d), T)
+    rows = T * K  # at least one bucketed row per (token, expert) pair
+    assert need >= rows * H * 2 + 2 * rows * I * 2 + 4 * rows * H * 4
+    # one token keeps the streaming kernel's much smaller workspace
+    assert lib.wr_fused_moe_workspace_size(ctypes.byref(d), 1) < rows * I * 2
+    # fp32 batches stay on the streaming kernel
+    d32 = _abi.desc(E, H, I, K, _abi.WR_DTYPE_F32)
+    assert lib.wr_fused_moe_workspace_size(ctypes.byref(d32), T) < need
+    # grows with the batch
+    assert lib.wr_fused_moe_workspace_size(ctypes.byref(d), 2 * T) > need
+
+
 def test_empty_batch_needs_no_gpu():
     lib = _abi.load()
     d = _desc()

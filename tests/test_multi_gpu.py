@@ -1,5 +1,7 @@
-"""The all-reduce fused into the layer (wr_fused_moe_allreduce / PeerComm),
-run as one child process per GPU on 2 GPUs (skipped with fewer).
+"""Multi-GPU layers, run as one child process per GPU on 2 GPUs (skipped with
+fewer): the all-reduce fused into the layer (wr_fused_moe_allreduce /
+PeerComm), and the expert-parallel token batch on the grouped tcgen05 path
+with an NCCL all-reduce (the batched sweep's 8-GPU layout).
 
 Each rank holds a tensor-parallel slice (or an expert-parallel set) of one
 layer; the fused call must return the full layer's output — compared with the
@@ -95,3 +97,54 @@ def test_fused_allreduce_matches_whole_layer(mode):
     import torch.multiprocessing as mp
 
     mp.spawn(_worker, args=(WORLD, _free_port(), mode), nprocs=WORLD, join=True)
+
+
+def _worker_batched_ep(rank: int, world: int, port: int) -> None:
+    import sys
+    from datetime import timedelta
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(repo, "warp-route_b200"))
+    import torch.distributed as dist
+
+    from warp_route import functional as F
+    from warp_route import synthetic
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        E, H, I, K = 8, 1024, 2048, 2
+        for T in (16, 100):
+            full = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=41, tokens=T,
+                                        router_bias=True)
+            shard = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=41, tokens=T,
+                                         router_bias=True, ep_rank=rank, ep_size=world)
+            out, ids, _ = F.fused_moe_routed(shard.x, shard.gate_w, shard.weight_buf, E, H, I, K,
+                                             router_bias=shard.router_bias,
+                                             ep_first_expert=shard.ep_first,
+                                             ep_num_local=shard.ep_num)
+            dist.all_reduce(out)
+            ref, ref_ids, _ = F.fused_moe_routed(full.x, full.gate_w, full.weight_buf, E, H, I, K,
+                                                 router_bias=full.router_bias)
+            torch.cuda.synchronize()
+            assert torch.equal(ids, ref_ids), f"rank {rank}: routing differs from the whole layer"
+            err = _rel_l2(out, ref)
+            assert err <= REL_L2_TOL, f"rank {rank} T={T}: rel L2 {err:.3e}"
+            # identical on both ranks
+            other = out.clone()
+            dist.broadcast(other, src=0)
+            torch.cuda.synchronize()
+            assert torch.equal(other, out), "ranks disagree after the all-reduce"
+        assert F._load_extension().workspace_status(out) == 0
+    finally:
+        dist.destroy_process_group()
+
+
+def test_batched_expert_parallel_matches_whole_layer():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker_batched_ep, args=(WORLD, _free_port()), nprocs=WORLD, join=True)
