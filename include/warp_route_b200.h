@@ -210,6 +210,28 @@ WR_API wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num
                                           void* workspace, size_t workspace_bytes,
                                           wr_comm_t comm, wr_stream_t stream);
 
+/* ---- weight packing ---------------------------------------------------- */
+
+/* Packs one rank's shard of the expert weights into the flat layout (see
+ * wr_expert_offsets) on the device, in one launch on `stream`: experts
+ * [ep_first, ep_first + ep_num) of num_experts, renumbered from slot 0, and
+ * of each the intermediate rows [tp_rank * I/tp_size, (tp_rank+1) * I/tp_size)
+ * of gate and up and the matching columns of down, packed with
+ * intermediate_dim = I / tp_size.  gate, up, down: host arrays of num_experts
+ * device pointers to row-major [I,H], [I,H], [H,I] matrices of `dtype`
+ * (entries outside the shard may be NULL).  dst: ep_num * expert stride
+ * bytes (dst_bytes); the stride-rounding bytes are zeroed.  ep_num <= 64.
+ * Replaces _pack_expert_weights (warp_route/functional.py:21-57), which
+ * packs the whole layer with one copy per matrix and has no per-rank
+ * slicing; the whole layer is ep_first = 0, ep_num = num_experts,
+ * tp_rank = 0, tp_size = 1. */
+WR_API wr_status_t wr_pack_experts(int32_t num_experts, int32_t hidden_dim,
+                                   int32_t intermediate_dim, int32_t dtype, int32_t ep_first,
+                                   int32_t ep_num, int32_t tp_rank, int32_t tp_size,
+                                   const void* const* gate, const void* const* up,
+                                   const void* const* down, void* dst, int64_t dst_bytes,
+                                   wr_stream_t stream);
+
 /* ---- naive multi-kernel layer ----------------------------------------- */
 
 /* Scratch bytes for wr_naive_moe.  Replaces naive_moe_alloc_scratch /

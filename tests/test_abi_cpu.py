@@ -151,3 +151,29 @@ def test_empty_batch_needs_no_gpu():
     st = lib.wr_batched_fused_moe(ctypes.byref(d), 0, FAKE, FAKE, FAKE, 0, None, None, None, None,
                                   0, None)
     assert st == _abi.WR_OK
+
+
+def test_pack_experts_argument_checks():
+    """wr_pack_experts rejects bad shards before touching any memory."""
+    lib = _abi.load()
+    P = ctypes.c_void_p * 8
+    ptrs = P(*([0x1000] * 8))
+    ok_args = dict(E=8, H=512, I=1024, dtype=_abi.WR_DTYPE_BF16, first=0, num=8, tpr=0, tps=1)
+
+    def call(**kw):
+        a = dict(ok_args, **kw)
+        return lib.wr_pack_experts(a["E"], a["H"], a["I"], a["dtype"], a["first"], a["num"],
+                                   a["tpr"], a["tps"], ptrs, ptrs, ptrs, FAKE,
+                                   kw.get("bytes", 1 << 40), None)
+
+    assert call(first=6, num=4) == _abi.WR_ERR_INVALID          # shard outside [0, E)
+    assert call(tps=3) == _abi.WR_ERR_INVALID                   # 3 does not divide I
+    assert call(tpr=2, tps=2) == _abi.WR_ERR_INVALID            # rank out of range
+    assert call(dtype=7) == _abi.WR_ERR_INVALID
+    need = 8 * lib.wr_total_weight_bytes(1, 512, 1024, 2)
+    assert call(bytes=need - 1) == _abi.WR_ERR_TOO_SMALL
+    assert "weight_buf too small" in lib.wr_last_error_string().decode()
+    empty = P(*([None] * 8))
+    st = lib.wr_pack_experts(8, 512, 1024, _abi.WR_DTYPE_BF16, 0, 8, 0, 1, empty, ptrs, ptrs,
+                             FAKE, need, None)
+    assert st == _abi.WR_ERR_INVALID                            # NULL matrix in the shard

@@ -32,7 +32,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
                      "-I" + INCLUDE, "-I" + CSRC]
 KERNEL_SOURCES = ["wr_api.cu", "wr_fused.cu", "wr_naive.cu", "wr_noalloc.cu", "wr_comm.cu",
-                  "wr_grouped.cu"]
+                  "wr_grouped.cu", "wr_pack.cu"]
 HEADERS = ["wr_common.cuh", "wr_router.cuh", "wr_internal.h"]
 
 

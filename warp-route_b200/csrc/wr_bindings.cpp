@@ -297,6 +297,58 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_moe_allreduce(
                     reinterpret_cast<wr_comm_t>(comm));
 }
 
+// One rank's shard of per-expert weight lists packed on the device
+// (wr_pack_experts): experts [ep_first, ep_first + ep_num), intermediate
+// slice tp_rank of tp_size.  Entries outside the shard are not read.
+torch::Tensor pack_experts(const std::vector<torch::Tensor>& gate,
+                           const std::vector<torch::Tensor>& up,
+                           const std::vector<torch::Tensor>& down, int num_experts,
+                           int hidden_dim, int intermediate_dim, int ep_first, int ep_num,
+                           int tp_rank, int tp_size) {
+  TORCH_CHECK((int)gate.size() == num_experts && (int)up.size() == num_experts &&
+                  (int)down.size() == num_experts,
+              "gate_proj, up_proj and down_proj must each hold num_experts=", num_experts,
+              " tensors");
+  TORCH_CHECK(ep_num >= 1 && ep_first >= 0 && ep_first + ep_num <= num_experts,
+              "expert shard [", ep_first, ", ", ep_first + ep_num, ") is outside [0, ",
+              num_experts, ")");
+  const torch::Tensor& ref = gate[ep_first];
+  CHECK_CUDA(ref);
+  CHECK_DTYPE(ref);
+  std::vector<const void*> g(num_experts, nullptr), u(num_experts, nullptr),
+      d(num_experts, nullptr);
+  for (int e = ep_first; e < ep_first + ep_num; ++e) {
+    const torch::Tensor* mats[3] = {&gate[e], &up[e], &down[e]};
+    const char* names[3] = {"gate_proj", "up_proj", "down_proj"};
+    for (int m = 0; m < 3; ++m) {
+      const torch::Tensor& t = *mats[m];
+      CHECK_CUDA(t);
+      CHECK_CONTIGUOUS(t);
+      check_same(ref, t, "gate_proj", names[m]);
+      const int64_t rows = m == 2 ? hidden_dim : intermediate_dim;
+      const int64_t cols = m == 2 ? intermediate_dim : hidden_dim;
+      TORCH_CHECK(t.dim() == 2 && t.size(0) == rows && t.size(1) == cols, names[m], "[", e,
+                  "] must have shape [", rows, ", ", cols, "], got shape ", t.sizes());
+    }
+    g[e] = gate[e].data_ptr();
+    u[e] = up[e].data_ptr();
+    d[e] = down[e].data_ptr();
+  }
+  TORCH_CHECK(tp_size >= 1 && intermediate_dim % tp_size == 0,
+              "tp_size must divide intermediate_dim");
+  const int elt = (int)ref.element_size();
+  const int64_t stride = wr_total_weight_bytes(1, hidden_dim, intermediate_dim / tp_size, elt);
+  const c10::cuda::CUDAGuard guard(ref.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(ref.device().index()).stream();
+  torch::Tensor buf = torch::empty({ep_num * stride / elt}, ref.options());
+  check_status(wr_pack_experts(num_experts, hidden_dim, intermediate_dim,
+                               ref.scalar_type() == torch::kBFloat16 ? WR_DTYPE_BF16
+                                                                     : WR_DTYPE_F32,
+                               ep_first, ep_num, tp_rank, tp_size, g.data(), u.data(), d.data(),
+                               buf.data_ptr(), ep_num * stride, stream));
+  return buf;
+}
+
 int64_t workspace_status(torch::Tensor hidden) {
   // Reads and clears the status word of this device/stream's cached workspace.
   const c10::cuda::CUDAGuard guard(hidden.device());
@@ -333,6 +385,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("hidden_dim"), py::arg("intermediate_dim"), py::arg("top_k"), py::arg("comm"),
         py::arg("router_bias") = py::none(), py::arg("ep_first_expert") = 0,
         py::arg("ep_num_local") = 0);
+  m.def("pack_experts", &pack_experts,
+        "Pack one rank's shard (experts, intermediate slice) of per-expert weights on the "
+        "device");
   m.def("workspace_status", &workspace_status,
         "Read and clear the device status word of the current stream's workspace");
   m.def("version", []() { return std::string(wr_version()); });

@@ -18,6 +18,7 @@ from .functional import (
     fused_moe_batched,
     fused_moe_routed,
     naive_moe,
+    pack_expert_shard,
     router_topk,
 )
 
@@ -29,6 +30,7 @@ __all__ = [
     "fused_moe_batched",
     "fused_moe_routed",
     "router_topk",
+    "pack_expert_shard",
     "_pack_expert_weights",
 ]
 

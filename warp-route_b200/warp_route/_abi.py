@@ -66,6 +66,9 @@ SIGNATURES = {
     "wr_naive_moe_workspace_size": (_sz, [_D]),
     "wr_naive_moe": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "wr_workspace_status": (_i32, [_vp, _vp]),
+    "wr_pack_experts": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                               ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                               _vp, _i64, _vp]),
     "wr_comm_handle_bytes": (_sz, []),
     "wr_comm_create": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_vp)]),
     "wr_comm_get_handle": (_i32, [_vp, _vp]),

@@ -60,6 +60,11 @@ def _pack_expert_weights(
     dtype = gate_proj[0].dtype
     if dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"expert weights must be float32 or bfloat16, got {dtype}")
+    if _device_packable(gate_proj, up_proj, down_proj, num_experts):
+        # one device launch for the whole buffer (wr_pack_experts)
+        return _load_extension().pack_experts(list(gate_proj), list(up_proj), list(down_proj),
+                                               num_experts, hidden_dim, intermediate_dim, 0,
+                                               num_experts, 0, 1)
     elt = torch.empty((), dtype=dtype).element_size()
     n = intermediate_dim * hidden_dim
     stride = _expert_stride_elems(hidden_dim, intermediate_dim, elt)
@@ -71,6 +76,63 @@ def _pack_expert_weights(
         buf[base + n:base + 2 * n] = up_proj[e].contiguous().view(-1).to(dtype)
         buf[base + 2 * n:base + 3 * n] = down_proj[e].contiguous().view(-1).to(dtype)
     return buf
+
+
+def _device_packable(gate_proj, up_proj, down_proj, num_experts: int) -> bool:
+    """All matrices CUDA, contiguous, of one dtype and device, and at most 64
+    experts: the device pack kernel takes them as they are."""
+    if num_experts > 64:
+        return False
+    ref = gate_proj[0]
+    if not ref.is_cuda:
+        return False
+    for lst in (gate_proj, up_proj, down_proj):
+        if len(lst) != num_experts:
+            return False
+        for t in lst:
+            if not (t.is_cuda and t.is_contiguous() and t.dtype == ref.dtype
+                    and t.device == ref.device and t.dim() == 2):
+                return False
+    return True
+
+
+def pack_expert_shard(
+    gate_proj: List[torch.Tensor],
+    up_proj: List[torch.Tensor],
+    down_proj: List[torch.Tensor],
+    num_experts: int,
+    hidden_dim: int,
+    intermediate_dim: int,
+    *,
+    tp_rank: int = 0,
+    tp_size: int = 1,
+    ep_rank: int = 0,
+    ep_size: int = 1,
+) -> Tuple[torch.Tensor, int, int, int]:
+    """One rank's shard of the layer, packed on the device in one launch.
+
+    Expert parallel: rank ep_rank of ep_size holds experts
+    [ep_rank*E/ep_size, (ep_rank+1)*E/ep_size), packed from slot 0.  Tensor
+    parallel: rank tp_rank of tp_size holds, of every expert, the intermediate
+    rows [tp_rank*I/tp_size, (tp_rank+1)*I/tp_size) of gate and up and the
+    matching columns of down.  The per-expert matrices (CUDA, contiguous,
+    float32 or bfloat16: gate/up [I,H], down [H,I]) stay where they are; only
+    the shard's experts are read.  Returns (weight_buf, ep_first_expert,
+    ep_num_local, intermediate_local): pass the last three to the fused entry
+    points (ep_num_local = 0 when the rank holds every expert).
+    """
+    if ep_size < 1 or num_experts % ep_size or not 0 <= ep_rank < ep_size:
+        raise ValueError(f"ep_size {ep_size} must divide num_experts {num_experts} "
+                         f"and 0 <= ep_rank < ep_size")
+    if tp_size < 1 or intermediate_dim % tp_size or not 0 <= tp_rank < tp_size:
+        raise ValueError(f"tp_size {tp_size} must divide intermediate_dim {intermediate_dim} "
+                         f"and 0 <= tp_rank < tp_size")
+    n = num_experts // ep_size
+    first = ep_rank * n
+    buf = _load_extension().pack_experts(list(gate_proj), list(up_proj), list(down_proj),
+                                         num_experts, hidden_dim, intermediate_dim, first, n,
+                                         tp_rank, tp_size)
+    return buf, (first if ep_size > 1 else 0), (n if ep_size > 1 else 0), intermediate_dim // tp_size
 
 
 def fused_moe(
