@@ -12,9 +12,10 @@ so every step streams weights from HBM (each step reads more than L2 holds).
 
 Rank 0 prints one JSON line.  `value` is µs per layer (max over ranks, CUDA
 events on the launching stream; the timed steps replay a CUDA graph of the
-layer calls); `e2e` is the same through the public API, eagerly, with the
-token copied in from pinned host memory and the output copied back every step
-(copies on their own streams, overlapping the kernels); `roofline` relates
+layer calls); `e2e` is the same through the public API with the token copied
+in from pinned host memory and the output copied back every step (copies on
+their own streams, overlapping the kernels; the steps replayed from CUDA
+graphs of 64 steps, or eagerly with --no-graph); `roofline` relates
 the fused kernel's algorithmic bytes to the
 measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
 composition (restated in oracle/torch_composition.py) on a bounded sample.
@@ -52,6 +53,7 @@ METRIC = "µs per MoE layer & achieved HBM GB/s, Mixtral shape bs=1, at 1/2/4/8 
 SHAPES = {"tiny": (8, 512, 1024, 2), "mixtral": (8, 4096, 14336, 2),
           "deepseek": (64, 2048, 1408, 6), "dbrx": (16, 6144, 10752, 4)}
 L2_BYTES = 126 * 1024 * 1024
+E2E_CHUNK = 64  # e2e steps per captured graph
 
 
 def parse():
@@ -526,14 +528,60 @@ def run_ours(args, world, rank, local):
     for i in range(min(W, 8)):
         e2e_step(i)
     torch.cuda.synchronize()
+    # Serving replays its steps from CUDA graphs: unless --no-graph, the timed
+    # e2e steps are replays of a graph of E2E_CHUNK steps, each step the same
+    # three operations (pinned-host -> device copy of its token, the public
+    # layer call, device -> pinned-host copy of its output) on the same three
+    # streams, ordered by the same events (graph edges after capture).
+    e2e_graphs = []
+    if use_graph:
+        cap2 = torch.cuda.Stream()
+        with torch.cuda.stream(cap2):  # the capture stream's workspace exists before capture
+            for Lr in layers:
+                layer(Lr, Lr.x)
+        torch.cuda.synchronize()
+
+        def capture_e2e(n):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap2):
+                h2d.wait_stream(cap2)
+                d2h.wait_stream(cap2)
+                for i in range(n):
+                    b, li = i % NB, i % n_layers
+                    with torch.cuda.stream(h2d):
+                        if i >= NB:
+                            h2d.wait_event(ev_read[b])
+                        x_dev[b].copy_(x_host[li], non_blocking=True)
+                        ev_in[b].record(h2d)
+                    cap2.wait_event(ev_in[b])
+                    o = layer(layers[li], x_dev[b])
+                    reduce(o)
+                    ev_read[b].record(cap2)
+                    with torch.cuda.stream(d2h):
+                        d2h.wait_event(ev_read[b])
+                        y_host[i % y_host.shape[0]].copy_(o, non_blocking=True)
+                cap2.wait_stream(h2d)
+                cap2.wait_stream(d2h)
+            return g
+
+        chunk = min(Ke, E2E_CHUNK)
+        g_e2e = capture_e2e(chunk)
+        rem = Ke % chunk
+        e2e_graphs = [g_e2e] * (Ke // chunk) + ([capture_e2e(rem)] if rem else [])
+        g_e2e.replay()
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    h2d.wait_event(e0)
-    for i in range(Ke):
-        e2e_step(i)
-    stream.wait_stream(d2h)
+    if use_graph:
+        for g in e2e_graphs:
+            g.replay()
+    else:
+        h2d.wait_event(e0)
+        for i in range(Ke):
+            e2e_step(i)
+        stream.wait_stream(d2h)
     e1.record(stream)
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], device=dev)
@@ -592,7 +640,9 @@ def run_ours(args, world, rank, local):
                          "algorithmic_bytes": int(avg_bytes)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/layer",
                     "h2d_bytes_per_step": H * elt * world,
-                    "d2h_bytes_per_step": H * 4 * world},
+                    "d2h_bytes_per_step": H * 4 * world,
+                    "timing": ("CUDA-graph replays of [H2D copy, layer call, D2H copy] steps"
+                               if use_graph else "eager steps")},
             "gpu_launches": Ksteps,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -128,6 +128,22 @@ WR_DEVINL uint64_t l2_policy_evict_last() {
   return p;
 }
 
+// Brings [p, p + bytes) into L2 without touching shared memory or L1
+// (p 16-byte aligned, bytes a multiple of 16).  L2 is the device's point of
+// coherence, so a prefetch never makes a later read see stale data.
+WR_DEVINL void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetches this CTA's share (CTA b of G) of [p, p + bytes) into L2, in
+// 16-byte-aligned pieces; p must be 16-byte aligned.
+WR_DEVINL void prefetch_share_l2(const void* p, int64_t bytes, int b, int G) {
+  const int64_t units = bytes >> 4;  // whole 16-byte units (a ragged tail is skipped)
+  const int64_t u0 = units * b / G, u1 = units * (b + 1) / G;
+  if (u1 > u0)
+    bulk_prefetch_l2(static_cast<const uint8_t*>(p) + (u0 << 4), (uint32_t)((u1 - u0) << 4));
+}
+
 // Orders this thread's generic-proxy accesses against later async-proxy
 // (bulk copy) accesses to global / shared memory.
 WR_DEVINL void fence_proxy_async_global() {

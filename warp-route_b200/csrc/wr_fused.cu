@@ -439,6 +439,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     fence_mbar_init();
   }
 
+  // The router's inputs into L2 while the previous kernel finishes (each CTA
+  // a share): gate_w does not depend on it, and x may, but a prefetch into
+  // L2 (the point of coherence) cannot return stale data later.
+  if (tid == 32 * W) {
+    prefetch_share_l2(a.gate_w, (int64_t)E * H * (kBf16 ? 2 : 4), b, G);
+    prefetch_share_l2(a.x, (int64_t)T * H * (kBf16 ? 2 : 4), b, G);
+  }
   // The previous kernel on the stream (which may have produced x, or be the
   // previous call on this workspace) is complete from here on.  The next
   // kernel may begin its launch now: its CTAs take over SMs as ours exit.
