@@ -79,6 +79,9 @@ def parse():
                     help="batched-decode sweep token counts; empty: no sweep")
     ap.add_argument("--sweep-layers", type=int, default=32)
     ap.add_argument("--sweep-steps", type=int, default=3)
+    ap.add_argument("--sweep-fused-allreduce", action="store_true",
+                    help="N > 1: sum the sweep's batch outputs in the layer's combine step "
+                         "over NVLink peer memory instead of NCCL (needs --allreduce fused)")
     ap.add_argument("--only-sweep", action="store_true",
                     help="run only the batched-decode sweep (N = 1) and print its JSON line")
     return ap.parse_args()
@@ -249,13 +252,14 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def batched_sweep(args, dev, world=1, rank=0):
+def batched_sweep(args, dev, world=1, rank=0, comm=None):
     """The batched-decode sweep (Mixtral shape, router bias, stacked layers):
     per token count, µs per layer over CUDA-graph replays of one step (every
     layer once) and the HBM GB/s of the distinct experts each layer streams.
     N > 1: expert parallel (rank r holds experts [r E/N, (r+1) E/N) of every
-    layer) and one NCCL all-reduce of the [T, H] output per layer, inside the
-    graph; the time is the max over ranks."""
+    layer) and the [T, H] output summed over the ranks per layer — by the
+    layer's own combine step over NVLink peer memory (comm, a PeerComm) or by
+    an NCCL all-reduce — inside the graph; the time is the max over ranks."""
     import torch.distributed as dist
 
     from warp_route import functional as F
@@ -291,6 +295,12 @@ def batched_sweep(args, dev, world=1, rank=0):
 
         def step():
             for Lr in layers:
+                if comm is not None:
+                    F.fused_moe_allreduce(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K, comm,
+                                          router_bias=Lr.router_bias,
+                                          ep_first_expert=Lr.ep_first,
+                                          ep_num_local=Lr.ep_num)
+                    continue
                 out = F.fused_moe_routed(xin, Lr.gate_w, Lr.weight_buf, E, H, I, K,
                                          router_bias=Lr.router_bias,
                                          ep_first_expert=Lr.ep_first,
@@ -341,8 +351,10 @@ def batched_sweep(args, dev, world=1, rank=0):
         results.append(r)
     del layers
     torch.cuda.empty_cache()
-    par = f"expert parallel over {world} GPUs ({E // world} experts each), NCCL all-reduce " \
-          f"of the [T,H] fp32 output in the graph" if world > 1 else "single GPU"
+    how = ("summed in the layer's combine step over NVLink peer memory" if comm is not None
+           else "NCCL all-reduce")
+    par = (f"expert parallel over {world} GPUs ({E // world} experts each), [T,H] fp32 output "
+           f"{how}, in the graph" if world > 1 else "single GPU")
     return {"config": "mixtral, router bias N(0,1), bf16", "layers": nl,
             "steps": args.sweep_steps, "parallelism": par,
             "note": "each layer has its own weights, gate and bias and takes the same seeded "
@@ -607,7 +619,12 @@ def run_ours(args, world, rank, local):
                          f"selected experts widened to fp32, median of {ncalls} after 3 warm-ups; "
                          f"warp-route's torch composition restated in oracle/torch_composition.py"}
 
-    sweep = batched_sweep(args, dev, world, rank)
+    # The sweep sums the ranks' batch outputs with NCCL: measured faster than the
+    # all-reducing combine step for batches (2 GPUs, 8 layers: 250 vs 260 µs
+    # at T = 16, 428 vs 456 µs at T = 256); `--sweep-fused-allreduce` uses the
+    # combine step instead.
+    sweep = batched_sweep(args, dev, world, rank,
+                          comm if args.sweep_fused_allreduce else None)
 
     if world > 1:
         dist.barrier()

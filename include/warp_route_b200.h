@@ -177,7 +177,7 @@ WR_API wr_status_t wr_batched_fused_moe(const wr_moe_desc_t* desc, int32_t num_t
  * step (no warp-route counterpart: warp-route is single-GPU; it replaces the
  * NCCL all-reduce a tensor- or expert-parallel caller would run after
  * fused_moe_forward).  Ranks are the GPUs of one node, one process each.
- * Set-up, once per process (allocates 512 * hidden_dim + 256 bytes of
+ * Set-up, once per process (allocates 8192 * hidden_dim + 256 bytes of
  * device memory on the current device):
  *   wr_comm_create -> wr_comm_get_handle -> exchange the world_size handles
  *   among the ranks (any host-side channel) -> wr_comm_open with all of them

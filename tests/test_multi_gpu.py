@@ -61,10 +61,14 @@ def _worker(rank: int, world: int, port: int, mode: str) -> None:
                                      ep_rank=rank if ep > 1 else 0, ep_size=ep)
         gen = torch.Generator(device="cuda")
         gen.manual_seed(77)
-        # several calls in a row (both parities of the peer buffers), then a
-        # batch of 6 tokens (two launches of at most 4 tokens)
+        # several calls in a row (both parities of the peer buffers), then
+        # batches on the grouped path, whose combine step sums the ranks'
+        # outputs (100 tokens: two all-reducing launches of <= 64 tokens),
+        # and single tokens again
         xs = [torch.randn(H, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(5)]
         xs.append(torch.randn(6, H, generator=gen, device="cuda").to(torch.bfloat16))
+        xs.append(torch.randn(100, H, generator=gen, device="cuda").to(torch.bfloat16))
+        xs += [torch.randn(H, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(2)]
         outs = []
         for x in xs:
             out = F.fused_moe_allreduce(x, shard.gate_w, shard.weight_buf, E, H, shard.I, K, comm,

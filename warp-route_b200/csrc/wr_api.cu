@@ -132,8 +132,8 @@ wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const
                       const CommView* comm = nullptr) {
   if (p.T == 0) return WR_OK;
   const bool ptr_ok = aligned16(x) && aligned16(gate_w) && aligned16(wbuf);
-  if (!comm && ptr_ok && grouped_supported(p))
-    return launch_grouped(p, x, gate_w, wbuf, out, ids, w, ws, stream);
+  if (ptr_ok && grouped_supported(p))
+    return launch_grouped(p, x, gate_w, wbuf, out, ids, w, ws, stream, comm);
   for (int t0 = 0; t0 < p.T; t0 += 4) {
     Problem q = p;
     q.T = p.T - t0 < 4 ? p.T - t0 : 4;

@@ -434,6 +434,102 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
   out[(int64_t)t * H4 + h] = acc;
 }
 
+// The combine with the ranks' outputs summed over NVLink peer memory, for
+// tokens [t0, t0 + Tc) (Tc <= kCommMaxTokens).  Each thread's (token, 4
+// columns) items: the partial output is written as words (fp32 | epoch << 32)
+// into this rank's slot of every rank's mailbox (relaxed system-scope
+// stores), then the words of every source rank are polled in this rank's
+// mailbox until they carry this launch's epoch and summed in rank order
+// (bit-identical on every rank).  An aligned 64-bit store is single-copy
+// atomic, so a word with the right epoch has the right value.  The grid is
+// small enough to be resident at once on every rank (no CTA waits for a
+// peer CTA that cannot run); the last CTA to finish publishes the epoch.
+constexpr int kCtlExit = 1;  // control word: CTAs done (the streaming kernel's, zero between launches)
+
+__global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ ypart,
+                                                    const int32_t* __restrict__ slot,
+                                                    const int2* __restrict__ row_tile,
+                                                    const int* __restrict__ meta, int K, int H,
+                                                    int rmax, int kcB, int grid, int jmax, int t0,
+                                                    int Tc, const CommView comm,
+                                                    uint32_t* __restrict__ ctl,
+                                                    float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ uint32_t s_ep;
+  if (threadIdx.x == 0) s_ep = *comm.epoch + 1;
+  __syncthreads();
+  const uint32_t ep = s_ep;
+  const SplitK sk = make_splitk(meta[2], kcB, grid, jmax);
+  const int H4 = H / 4;
+  const int items = Tc * H4;
+  const int stride = gridDim.x * blockDim.x;
+  const uint64_t tag = (uint64_t)ep << 32;
+  for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const int tl = it / H4, h4 = it - tl * H4;
+    const int t = t0 + tl;
+    const int mt = (h4 * 4) / kRowsB;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const int r = slot[(int64_t)t * K + k];
+      if (r < 0) continue;
+      const int2 rt = row_tile[r];
+      const int tile = rt.x + mt * rt.y;
+      const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
+      for (int j = 0; j <= c1 - c0; ++j) {
+        const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h4];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    const size_t off =
+        (((size_t)comm.rank * 2 + (ep & 1u)) * kCommMaxTokens + tl) * (size_t)H + 4 * h4;
+    for (int q = 0; q < comm.world; ++q) {
+      uint64_t* d = comm.box[q] + off;
+      st_relaxed_sys_u64(d + 0, tag | __float_as_uint(acc.x));
+      st_relaxed_sys_u64(d + 1, tag | __float_as_uint(acc.y));
+      st_relaxed_sys_u64(d + 2, tag | __float_as_uint(acc.z));
+      st_relaxed_sys_u64(d + 3, tag | __float_as_uint(acc.w));
+    }
+  }
+  const uint64_t tstart = globaltimer_ns();
+  bool late = false;
+  for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += stride) {
+    const int tl = it / H4, h4 = it - tl * H4;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < comm.world; ++q) {
+      const uint64_t* p = comm.box[comm.rank] +
+                          (((size_t)q * 2 + (ep & 1u)) * kCommMaxTokens + tl) * (size_t)H + 4 * h4;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint64_t wv = ld_relaxed_sys_u64(p + c);
+        for (uint32_t spin = 1; (uint32_t)(wv >> 32) != ep && !late; ++spin) {
+          if ((spin & 63u) == 0 && globaltimer_ns() - tstart > kWaitLimitNs) {
+            atomicOr(ctl + 2, DEV_TIMEOUT_PEER);
+            late = true;
+          }
+          wv = ld_relaxed_sys_u64(p + c);
+        }
+        o[c] += __uint_as_float((uint32_t)wv);
+      }
+    }
+    *reinterpret_cast<float4*>(out + (int64_t)(t0 + tl) * H + 4 * h4) =
+        make_float4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(ctl + kCtlExit, 1u);
+    if (prev == gridDim.x - 1) {  // every CTA has left its waits
+      *comm.epoch = ep;          // the next launch uses epoch + 1
+      atomicExch(ctl + kCtlExit, 0u);
+      __threadfence();
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Grouped GEMM
 // ---------------------------------------------------------------------------
@@ -1104,7 +1200,8 @@ bool grouped_supported(const Problem& p) {
 size_t grouped_workspace_bytes(const Problem& p) { return make_plan(p).total; }
 
 wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, const void* wbuf,
-                           float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream) {
+                           float* out, int32_t* ids, float* w, void* ws, cudaStream_t stream,
+                           const CommView* comm) {
   const int sms = device_sm_count();
   const GroupedPlan g = make_plan(p);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
@@ -1209,6 +1306,20 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (down) launch");
 
   const int H4 = p.H / 4;
+  if (comm) {
+    // all-reduce in the combine, one launch (one epoch) per kCommMaxTokens tokens
+    for (int t0 = 0; t0 < p.T; t0 += kCommMaxTokens) {
+      const int Tc = p.T - t0 < kCommMaxTokens ? p.T - t0 : kCommMaxTokens;
+      int blocks = (Tc * H4 + 255) / 256;
+      if (blocks > 4 * sms) blocks = 4 * sms;
+      ce = launch_pdl(k_combine_ar, dim3(blocks), dim3(256), 0, stream,
+                      reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
+                      (const int2*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
+                      g.jmaxB, t0, Tc, *comm, reinterpret_cast<uint32_t*>(ws), out);
+      if (ce != cudaSuccess) return cuda_fail(ce, "combine (all-reduce) launch");
+    }
+    return WR_OK;
+  }
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
                   (const int2*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,

@@ -17,7 +17,7 @@ constexpr size_t kWsControlBytes = 512;
 
 // ---- peer-memory all-reduce (wr_comm.cu) ----
 constexpr int kMaxRanks = 8;
-constexpr int kCommMaxTokens = 4;   // tokens of one kernel launch
+constexpr int kCommMaxTokens = 64;  // tokens one kernel launch all-reduces
 
 // What the fused kernel needs of a communicator: every rank's mailbox,
 // mapped into this process, and this rank's launch counter.  A mailbox is
@@ -64,9 +64,11 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
 constexpr int kGroupedMinTokens = 2;
 bool grouped_supported(const Problem& p);
 size_t grouped_workspace_bytes(const Problem& p);
+// comm: null, or the communicator whose ranks' partial outputs the combine
+// step sums over peer memory (identical on every rank).
 wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w,
                            const void* wbuf, float* out, int32_t* ids, float* w, void* ws,
-                           cudaStream_t stream);
+                           cudaStream_t stream, const CommView* comm = nullptr);
 
 // ---- router kernel (wr_naive.cu) ----
 wr_status_t launch_router(const Problem& p, const void* x, const void* gate_w,
