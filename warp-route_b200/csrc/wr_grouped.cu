@@ -1,11 +1,11 @@
-// wr_grouped.cu — the batched layer for larger token batches as two grouped
+// wr_grouped.cu — the batched layer (two or more bf16 tokens) as two grouped
 // GEMMs on the 5th-generation tensor cores.
 //
 // warp-route's batched kernel (src/fused_moe_batched.cu:20-183) gives every
 // token its own CTA and streams every selected expert's weights once per
 // token, on CUDA cores.  Here the tokens are bucketed per expert first, so
 // each expert's weights stream from HBM once per batch and meet all of that
-// expert's tokens in a tcgen05 MMA:
+// expert's tokens in tcgen05 MMAs:
 //
 //   k_router        ids / weights of every token (bit-exact with the fused
 //                   path: same kernel as wr_router_topk)
@@ -14,32 +14,36 @@
 //                   multiple of 16 rows with zero-weight rows
 //   k_gather        X_g[row] = x[token of row] (bf16), zero for padding
 //   k_grouped_gemm<gate/up>
-//                   per (expert, 128 rows of I, <=128 tokens): gate and up
-//                   accumulators in TMEM over K = H, epilogue
-//                   act = silu(g) * u * w(token, k) stored as bf16 hi + lo
+//                   tile = (expert, 128 intermediate rows, <= 128 tokens):
+//                   D[token, 256] = X_g rows x [128 gate rows; 128 up rows],
+//                   epilogue act = silu(g) * u * w(token, k) stored as bf16
+//                   hi + lo (~16 mantissa bits for the second GEMM)
 //   k_grouped_gemm<down>
-//                   per (expert, 128 rows of H, <=128 tokens): Wd . act_hi +
-//                   Wd . act_lo (the hi/lo pair keeps the activation to ~16
-//                   mantissa bits); the K chunks of all tiles are dealt to
-//                   the CTAs in equal ranges (stream-K), a tile cut by a
-//                   range boundary leaves one fp32 partial per CTA
+//                   tile = (expert, 256 rows of H, <= 64 / 128 tokens):
+//                   D[token, 256] = [act_hi; act_lo] x Wd rows (hi and lo
+//                   stacked in one 128-row A tile, or two A tiles above 64
+//                   tokens), fp32 partials per K split
 //   k_combine       out[t] = sum over k (ascending) of the partials of its
-//                   row (in CTA order): one fixed order, so the result is
-//                   deterministic.
+//   (k_combine_ar)  rows (in CTA order): deterministic; with a communicator
+//                   the ranks' outputs are also summed over NVLink peer
+//                   memory, in rank order.
 //
-// GEMM structure: weights are the MMA's A operand (M = 128 weight rows,
-// K-major: rows of the packed layout are contiguous along K), tokens the B
-// operand (N = 16..128, K-major), both bf16, accumulator fp32 in TMEM.  One
-// persistent CTA per SM, 7 warps: warp 0 issues the weight TMA loads into a
-// deep ring (they come from HBM), warp 6 the token-tile loads into a shallow
-// ring (they come from L2), both 128-byte swizzled; warp 1 owns TMEM and
-// issues the MMAs (one elected lane, tcgen05.commit to release smem stages
-// and to hand accumulators to the epilogue); warps 2-5 read the accumulators
-// back with tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..+31) and store the
-// results.  Two accumulator buffers let the epilogue of one tile overlap the
-// MMAs of the next.  No TMA multicast anywhere; every wait is bounded and a
-// wait that runs out sets the workspace status word and winds the CTA down
-// (copies in flight drained, MMAs completed, TMEM freed).
+// GEMM structure: the tokens are the MMA's A operand (M = 128 token rows, of
+// which a tile's n are loaded), the weights its B operand (N = 256 weight
+// rows: one MMA consumes 256 rows x 16 K of weights whatever the token
+// count), both K-major bf16 (rows of the packed layout are contiguous along
+// K), accumulator fp32 in TMEM.  One persistent CTA per SM, 7 warps: warp 0
+// issues the weight TMA loads into a deep ring (they come from HBM), warp 6
+// the token-tile loads into a shallow ring (they come from L2), both
+// 128-byte swizzled; warp 1 owns TMEM and issues the MMAs (one elected lane,
+// tcgen05.commit to release smem stages and to hand accumulators to the
+// epilogue); warps 2-5 read the accumulators back with tcgen05.ld (warp w
+// reads TMEM lanes 32*(w%4)..+31) and store the results.  Two accumulator
+// buffers let the epilogue of one tile overlap the MMAs of the next.  The
+// K chunks of all tiles are dealt to the CTAs in equal ranges (stream-K).
+// No TMA multicast anywhere; every wait is bounded and a wait that runs out
+// sets the workspace status word and winds the CTA down (copies in flight
+// drained, MMAs completed, TMEM freed).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -242,10 +246,10 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 // token order, followed by zero-weight padding up to a multiple of 16.
 // Pairs of other ranks' experts get slot -1.  Each row also gets its first
 // down tile and the tile stride between H tiles (row_tile), which the
-// combine uses.  Zeroes the gate/up tile
-// counters (robust against a call that gave up half-way).  Also writes the tile counts
-// the GEMM kernels walk: per expert ntlA (ntlB) token tiles of <= nmaxA
-// (nmaxB) rows, mtA * ntlA gate/up tiles and mtB * ntlB down tiles.
+// combine uses.  Writes the tile counts the GEMM kernels walk (per expert
+// ntlA / ntlB token tiles of <= nmaxA / nmaxB rows; mtA * ntlA gate/up and
+// mtB * ntlB down tiles) and zeroes the gate/up tile counters (robust against
+// a call that gave up half-way).
 __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
                                                 const float* __restrict__ w, int TK, int K,
                                                 int ep_first, int E, int nmaxA, int nmaxB,
@@ -570,12 +574,10 @@ struct Work {
   }
 };
 
-// The sequence of work one CTA runs; every role of the CTA walks the same
-// sequence.  Gate/up: tiles blockIdx.x, blockIdx.x + gridDim.x, ... (each
-// whole).  Down: this CTA's stream-K chunk range.  Tiles are numbered
-// expert-major; inside an expert the token tile varies fastest (tiles that
-// share weights run on neighbouring CTAs at the same time, so the second
-// read mostly hits L2), then the weight-row tile.
+// The sequence of work one CTA runs (its stream-K chunk range, cut at tile
+// boundaries); every role of the CTA walks the same sequence.  Tiles are
+// numbered expert-major; inside an expert the token tile varies fastest,
+// then the weight-row tile.
 template <bool kGU>
 struct WorkIter {
   int64_t u, u1;
@@ -679,8 +681,10 @@ WR_DEVINL void swiglu_store16(const float (&g)[16], const float (&u)[16], float 
 // gate/up: B rows 0..127 = gate rows m0.., 128..255 = up rows m0.., so
 //   accumulator lane t (token) holds gate and up of the same rows in columns
 //   c and 128 + c: SwiGLU runs in the thread that owns the token.
-// down:    A rows 0..63 = act_hi of the tile's tokens, 64..127 = act_lo, so
-//   lane t and lane 64 + t hold the two halves of token t's output.
+// down:    up to 64 tokens: A rows 0..n-1 = act_hi of the tile's tokens,
+//   rows n_max.. = act_lo, so lanes t and n_max + t hold the two halves of
+//   token t's output; above 64 tokens: act_hi and act_lo are two 128-row A
+//   tiles, two MMAs per K step into the same accumulator.
 //
 // Warp roles: 0 weight loads, 6 token loads (one elected lane each), 1 TMEM
 // owner + MMA issue (one elected lane), 2..5 epilogue (TMEM lane quarter
