@@ -112,6 +112,8 @@ def test_hot_expert_spans_several_token_tiles():
 
 @pytest.mark.parametrize("E,H,I,K,T", [
     (8, 1000, 1000, 2, 20),    # row tiles and K chunks with tails (TMA zero fill)
+    (4, 64, 64, 2, 8),         # one K chunk, one row tile smaller than the MMA
+    (64, 256, 128, 8, 40),     # the most experts, top_k 8: many small buckets
     (4, 512, 768, 4, 32),      # top_k == E: every expert takes every token
     (8, 512, 1024, 1, 48),     # top_k == 1
     (3, 256, 512, 2, 16),      # odd expert count, smallest grouped batch
@@ -187,3 +189,14 @@ def test_python_api_matches_c_abi():
     b = F.batched_fused_moe(L.x, L.gate_w, L.weight_buf, E, H, I, K)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def test_many_pairs_bucket_reads_global():
+    """More (token, expert) pairs than the bucket kernel stages in shared
+    memory (T * K > 5632): its passes read the routing from global memory."""
+    E, H, I, K, T = 16, 256, 256, 8, 720  # 5760 pairs
+    L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=61, tokens=T,
+                             router_bias=True)
+    out, ids, w = _run(L, E, H, I, K)
+    _check_routing(ids, w, L, K)
+    _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, 1, 357, 719], L.router_bias)
