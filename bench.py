@@ -340,8 +340,11 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
         torch.cuda.synchronize()
         mean_distinct = sum(distinct) / len(distinct)
         wbytes = mean_distinct * 3 * H * I * 2
+        gbs = wbytes / (us * 1e-6) / 1e9
+        peak, _ = peaks()
         r = {"tokens": T, "us_per_layer": round(us, 2),
-             "hbm_gbs": round(wbytes / (us * 1e-6) / 1e9, 1),
+             "hbm_gbs": round(gbs, 1),
+             "frac_of_hbm_peak": round(gbs / (peak * world), 4),
              "experts_per_layer": round(mean_distinct, 2),
              "path": "streaming kernel" if T == 1 else "grouped tcgen05 GEMMs",
              "clocks": clk.summary()}
@@ -359,7 +362,8 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
             "steps": args.sweep_steps, "parallelism": par,
             "note": "each layer has its own weights, gate and bias and takes the same seeded "
                     "token batch; value = µs per layer (graph replays of the layer stack, max "
-                    "over ranks); hbm_gbs = distinct selected experts' weight bytes / time",
+                    "over ranks); hbm_gbs = distinct selected experts' weight bytes / time; "
+                    "frac_of_hbm_peak = hbm_gbs / (N x measured HBM bandwidth)",
             "results": results}
 
 
