@@ -7,11 +7,11 @@
 // each expert's weights stream from HBM once per batch and meet all of that
 // expert's tokens in tcgen05 MMAs:
 //
-//   k_router        ids / weights of every token (bit-exact with the fused
-//                   path: same kernel as wr_router_topk)
-//   k_bucket        (token, k) pairs of this rank's experts -> rows of a
-//                   per-expert token list, each expert's list padded to a
-//                   multiple of 16 rows with zero-weight rows
+//   k_route_bucket  one CTA per token: ids / weights (the router of
+//                   wr_router.cuh, bit-exact with wr_router_topk); the last
+//                   CTA buckets the (token, k) pairs of this rank's experts
+//                   into per-expert token lists, each padded to a multiple
+//                   of 16 rows with zero-weight rows
 //   k_gather        X_g[row] = x[token of row] (bf16), zero for padding
 //   k_grouped_gemm<gate/up>
 //                   tile = (expert, 128 intermediate rows, <= 128 tokens):
@@ -83,12 +83,12 @@ constexpr int kMaxTStages = 4;           // token ring depth limit
 // barriers (full/empty of both rings, 2 x accumulator full/empty, drain) and
 // three words (TMEM address, abort, fixup flag) in the first 512 bytes
 static_assert((2 * kMaxWStages + 2 * kMaxTStages + 5) * 8 + 12 <= 512, "barrier area");
-constexpr int kBucketSmemIds = 5632;    // k_bucket stages up to this many ids + weights (44 KB)
+constexpr int kBucketSmemIds = 5632;    // bucketing stages up to this many ids + weights (44 KB)
 constexpr int kJMaxA = 3;                // gate/up: CTAs sharing one tile, at most
 constexpr int kJMaxB = 4;                // down: partial sums per output tile, at least this cap
 constexpr int kJMaxBLimit = 16;          // ... and at most this one (few tiles: expert parallel)
 
-// Bucket metadata (int32 words in the workspace), written by k_bucket:
+// Bucket metadata (int32 words in the workspace), written by the bucketing:
 //   [0] rows in use, [1] gate/up tiles, [2] down tiles, and from word 16
 //   cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
 //   preA[E+1], preB[E+1] (tiles before each expert).
@@ -250,38 +250,65 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 // ntlA / ntlB token tiles of <= nmaxA / nmaxB rows; mtA * ntlA gate/up and
 // mtB * ntlB down tiles) and zeroes the gate/up tile counters (robust against
 // a call that gave up half-way).
-__global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
-                                                const float* __restrict__ w, int TK, int K,
-                                                int ep_first, int E, int nmaxA, int nmaxB,
-                                                int mtA, int mtB, int* __restrict__ meta,
-                                                int32_t* __restrict__ slot,
-                                                int32_t* __restrict__ row_tok,
-                                                int2* __restrict__ row_tile,
-                                                float* __restrict__ row_w,
-                                                uint32_t* __restrict__ tile_cnt, int cnt_words) {
-  extern __shared__ int s_ids[];  // ids, then weights, staged here when TK <= kBucketSmemIds
+struct BucketArgs {
+  const int32_t* ids;  // [TK], written by the routing CTAs of the same launch
+  const float* w;
+  int TK, K, ep_first, E, nmaxA, nmaxB, mtA, mtB;
+  int* meta;
+  int32_t* slot;
+  int32_t* row_tok;
+  int2* row_tile;
+  float* row_w;
+  uint32_t* tile_cnt;
+  int cnt_words;
+};
+
+// Run by one whole CTA.  s_ids: dynamic shared memory of 8 * TK bytes when
+// TK <= kBucketSmemIds (the ids, then the weights, are staged there).  The
+// ids and weights were written by other CTAs of this launch: read through L2.
+__device__ void bucket_body(const BucketArgs& b, int* s_ids) {
+  const int32_t* __restrict__ ids = b.ids;
+  const float* __restrict__ w = b.w;
+  const int TK = b.TK, K = b.K, ep_first = b.ep_first, E = b.E;
+  const int nmaxA = b.nmaxA, nmaxB = b.nmaxB, mtA = b.mtA, mtB = b.mtB;
+  int* __restrict__ meta = b.meta;
+  int32_t* __restrict__ slot = b.slot;
+  int32_t* __restrict__ row_tok = b.row_tok;
+  int2* __restrict__ row_tile = b.row_tile;
+  float* __restrict__ row_w = b.row_w;
+  uint32_t* __restrict__ tile_cnt = b.tile_cnt;
+  const int cnt_words = b.cnt_words;
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_base[kMaxExperts];
   __shared__ int s_preB[kMaxExperts];
   __shared__ int s_ntlB[kMaxExperts];
-  griddep_wait();
-  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const bool staged = TK <= kBucketSmemIds;
   for (int i = threadIdx.x; i < cnt_words; i += blockDim.x) tile_cnt[i] = 0u;
   float* s_w = reinterpret_cast<float*>(s_ids + TK);
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
-    const int id = ids[i];
+    const int id = __ldcg(ids + i);
     if (staged) {
       s_ids[i] = id;
-      s_w[i] = w[i];
+      s_w[i] = __ldcg(w + i);
     }
     const int e = id - ep_first;
     if (e < 0 || e >= E) slot[i] = -1;
   }
   __syncthreads();
-  const int* sid = staged ? s_ids : ids;
-  const float* sw = staged ? s_w : w;
+  // (unstaged: the routing is read through L2 again; it was written by other CTAs)
+  struct Src {
+    const int* p;
+    bool smem;
+    WR_DEVINL int operator[](int i) const { return smem ? p[i] : __ldcg(p + i); }
+  };
+  struct SrcF {
+    const float* p;
+    bool smem;
+    WR_DEVINL float operator[](int i) const { return smem ? p[i] : __ldcg(p + i); }
+  };
+  const Src sid{staged ? s_ids : ids, staged};
+  const SrcF sw{staged ? s_w : w, staged};
   for (int e = warp; e < E; e += nw) {
     int c = 0;
     for (int j = 0; j < TK; j += 32) {
@@ -346,6 +373,56 @@ __global__ void __launch_bounds__(512) k_bucket(const int32_t* __restrict__ ids,
       row_w[r] = 0.0f;
     }
   }
+}
+
+// Router and bucketing in one launch: CTA t computes token t's logits,
+// softmax and top-K (the router of wr_router.cuh, bit-exact with
+// wr_router_topk: warp j computes segment j of every router row, reading x
+// in 16-byte vectors), writes ids / weights, and counts itself in; the last
+// CTA to finish (no waiting) buckets every token.
+constexpr int kRouteThreads = 32 * kRouterSegments;
+constexpr int kCtlRoute = 4;  // control word: routing CTAs done (zero between launches)
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_bucket(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ gate_w,
+    const float* __restrict__ bias, int E_all, int H, bool vec_ok, uint32_t* __restrict__ ctl,
+    int32_t* __restrict__ ids_out, float* __restrict__ w_out, const BucketArgs b) {
+  extern __shared__ int s_dyn[];
+  __shared__ float parts[kRouterSegments * kMaxExperts];
+  __shared__ float lg[kMaxExperts];
+  __shared__ int tids[kMaxExperts];
+  __shared__ float tws[kMaxExperts];
+  __shared__ int s_last;
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = b.K;
+  router_segment_warp<uint16_t>(gate_w, XGlobal<uint16_t>{x + (int64_t)t * H}, E_all, H, warp,
+                                lane, vec_ok, parts + warp * kMaxExperts);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E_all; e += blockDim.x)
+    lg[e] = router_combine(parts, kMaxExperts, e, bias);
+  __syncthreads();
+  if (warp == 0) {
+    select_topk_warp(lg, E_all, K, lane, tids, tws);
+    __syncwarp();
+    for (int k = lane; k < K; k += 32) {
+      ids_out[(int64_t)t * K + k] = tids[k];
+      w_out[(int64_t)t * K + k] = tws[k];
+    }
+    __threadfence();  // this token's routing is visible before it is counted in
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(ctl + kCtlRoute, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  bucket_body(b, s_dyn);
+  if (threadIdx.x == 0) ctl[kCtlRoute] = 0u;  // ready for the next call
 }
 
 // X_g[row, :] = x[row_tok[row], :] (bf16, 16-byte chunks), zero for padding.
@@ -553,7 +630,7 @@ struct GemmArgs {
   float* ypart;        // down output: [jmax][rmax][H] fp32
   int jmax;            // CTAs per tile, at most (gate/up: kJMaxA)
   float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32
-  uint32_t* cnt;       // gate/up: CTAs done with each cut tile (zeroed by k_bucket)
+  uint32_t* cnt;       // gate/up: CTAs done with each cut tile (zeroed by the bucketing)
   uint32_t* status;
 };
 
@@ -1223,15 +1300,33 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   uint32_t* tcnt = reinterpret_cast<uint32_t*>(wsb + g.off_cnt);
   uint32_t* status = reinterpret_cast<uint32_t*>(ws) + 2;
 
-  wr_status_t st = launch_router(p, x, gate_w, nullptr, ids_d, w_d, stream);
-  if (st != WR_OK) return st;
+  wr_status_t st = WR_OK;
   const int TK = p.T * p.K;
   const size_t bucket_smem = TK <= kBucketSmemIds ? 8 * (size_t)TK : 0;
-  cudaError_t ce = launch_pdl(k_bucket, dim3(1), dim3(512), bucket_smem, stream,
-                              (const int32_t*)ids_d,
-                              (const float*)w_d, p.T * p.K, p.K, p.ep_first, p.ep_num, g.nmaxA,
-                              g.nmaxB, g.mtA, g.mtB, meta, slot, rtok, rtile, rw, tcnt,
-                              g.cnt_words);
+  BucketArgs ba;
+  ba.ids = ids_d;
+  ba.w = w_d;
+  ba.TK = TK;
+  ba.K = p.K;
+  ba.ep_first = p.ep_first;
+  ba.E = p.ep_num;
+  ba.nmaxA = g.nmaxA;
+  ba.nmaxB = g.nmaxB;
+  ba.mtA = g.mtA;
+  ba.mtB = g.mtB;
+  ba.meta = meta;
+  ba.slot = slot;
+  ba.row_tok = rtok;
+  ba.row_tile = rtile;
+  ba.row_w = rw;
+  ba.tile_cnt = tcnt;
+  ba.cnt_words = g.cnt_words;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(gate_w) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // H % 8 == 0 here
+  cudaError_t ce = launch_pdl(k_route_bucket, dim3(p.T), dim3(kRouteThreads), bucket_smem,
+                              stream, static_cast<const uint16_t*>(x),
+                              static_cast<const uint16_t*>(gate_w), p.router_bias, p.E, p.H,
+                              vec_ok, reinterpret_cast<uint32_t*>(ws), ids_d, w_d, ba);
   const int gather_blocks = g.rmax < 4 * sms ? g.rmax : 4 * sms;
   if (ce == cudaSuccess)
     ce = launch_pdl(k_gather, dim3(gather_blocks), dim3(256), 0, stream,
