@@ -67,7 +67,8 @@ constexpr int kNMaxB = 64;               // tokens per down tile, act_hi and act
 constexpr int kNMaxBSplit = 128;         // tokens per down tile, act_hi and act_lo as two A tiles
 constexpr int kRowB = kBK * 2;           // bytes of one row per stage
 constexpr int kWBox = 128;               // weight rows per TMA box
-constexpr int kBoxRows = 16;             // token rows per TMA box
+constexpr int kBoxRows = 16;             // token rows: tiles are multiples of this
+constexpr int kTokMaps = kTokM / kBoxRows;  // token maps with boxes of 16, 32, .., 128 rows
 constexpr int kWStageBytes = kWRows * kRowB;  // 32 KB
 constexpr int kTokBytes = kTokM * kRowB;      // 16 KB: the rows one MMA reads as A
 constexpr int kGemmThreads = 224;        // 7 warps
@@ -767,10 +768,17 @@ WR_DEVINL void swiglu_store16(const float (&g)[16], const float (&u)[16], float 
 // owner + MMA issue (one elected lane), 2..5 epilogue (TMEM lane quarter
 // warp % 4).  Weights and tokens have separate smem rings: weights come from
 // HBM and need a deep ring, token tiles come from L2 and a shallow one does.
+// One token tensor map per tile height: a tile of n rows (a multiple of 16)
+// is one TMA box of exactly n rows (every copy instruction costs the single
+// issuing thread time in each K step, so 16-row boxes slowed large tiles).
+struct TokenMaps {
+  CUtensorMap m[kTokMaps];  // m[h - 1]: boxes of 16 h rows
+};
+
 template <bool kGU>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_b, const GemmArgs a) {
+                   const __grid_constant__ TokenMaps tm_b, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   griddep_launch_dependents();
 
@@ -811,7 +819,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     *abort = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_w);
-    prefetch_tmap(&tm_b);
+    for (int h = 0; h < kTokMaps; ++h) prefetch_tmap(&tm_b.m[h]);
   }
   // Everything above touches only this CTA; the previous kernel's outputs
   // (bucket metadata, gathered tokens, activations) are read from here on.
@@ -867,15 +875,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_load_3d(s + kWBox * kRowB, &tm_w, kx, kGU ? a.I + w.m0 : w.m0 + kWBox, w.e,
                         &full[st], pol);
           } else {
-            for (int r = 0; r < nbox; ++r)
-              tma_load_2d(s + r * kBoxRows * kRowB, &tm_b, kx, w.row0 + r * kBoxRows, &full[st],
-                          pol);
-            if (!kGU) {  // act_lo rows at tile rows nmax.. (stacked) or in the second A tile
-              uint8_t* sl = s + (a.hl_split ? kTokM : a.nmax) * kRowB;
-              for (int r = 0; r < nbox; ++r)
-                tma_load_2d(sl + r * kBoxRows * kRowB, &tm_b, kx, a.rmax + w.row0 + r * kBoxRows,
-                            &full[st], pol);
-            }
+            const CUtensorMap* tm = &tm_b.m[nbox - 1];
+            tma_load_2d(s, tm, kx, w.row0, &full[st], pol);
+            if (!kGU)  // act_lo rows at tile rows nmax.. (stacked) or in the second A tile
+              tma_load_2d(s + (a.hl_split ? kTokM : a.nmax) * kRowB, tm, kx, a.rmax + w.row0,
+                          &full[st], pol);
           }
           ++issued;
           if (++st == stages) {
@@ -1159,6 +1163,24 @@ wr_status_t encode_map(CUtensorMap* m, const void* base, int rank, const cuuint6
   return WR_OK;
 }
 
+// Token maps with boxes of 16, 32, .. rows.  Heights above the largest tile
+// (nmax, and never above the rows a tile can start in) are never used and
+// repeat the 16-row map.
+wr_status_t encode_token_maps(TokenMaps* t, const void* base, const cuuint64_t* dims,
+                              const cuuint64_t* str, int nmax, int rmax) {
+  for (int h = 1; h <= kTokMaps; ++h) {
+    const int rows = h * kBoxRows;
+    if (h > 1 && (rows > nmax || rows > rmax)) {
+      t->m[h - 1] = t->m[0];
+      continue;
+    }
+    const cuuint32_t box[2] = {kBK, (cuuint32_t)rows};
+    const wr_status_t st = encode_map(&t->m[h - 1], base, 2, dims, str, box);
+    if (st != WR_OK) return st;
+  }
+  return WR_OK;
+}
+
 size_t a256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Everything the grouped path derives from the problem on the host.
@@ -1336,7 +1358,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
 
   const Layout lay = make_layout(p.H, p.I, 2);
   const uint8_t* wb = static_cast<const uint8_t*>(wbuf);
-  CUtensorMap tm_gu, tm_x, tm_dn, tm_act;
+  CUtensorMap tm_gu, tm_dn;
+  TokenMaps tm_x, tm_act;
   {
     const cuuint64_t dims[3] = {(cuuint64_t)p.H, (cuuint64_t)2 * p.I, (cuuint64_t)p.ep_num};
     const cuuint64_t str[2] = {(cuuint64_t)p.H * 2, (cuuint64_t)lay.stride};
@@ -1346,8 +1369,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.H, (cuuint64_t)g.rmax};
     const cuuint64_t str[1] = {(cuuint64_t)p.H * 2};
-    const cuuint32_t box[2] = {kBK, kBoxRows};
-    if ((st = encode_map(&tm_x, xg, 2, dims, str, box)) != WR_OK) return st;
+    if ((st = encode_token_maps(&tm_x, xg, dims, str, g.nmaxA, g.rmax)) != WR_OK) return st;
   }
   {
     const cuuint64_t dims[3] = {(cuuint64_t)p.I, (cuuint64_t)p.H, (cuuint64_t)p.ep_num};
@@ -1358,8 +1380,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.I, (cuuint64_t)2 * g.rmax};
     const cuuint64_t str[1] = {(cuuint64_t)p.I * 2};
-    const cuuint32_t box[2] = {kBK, kBoxRows};
-    if ((st = encode_map(&tm_act, act, 2, dims, str, box)) != WR_OK) return st;
+    if ((st = encode_token_maps(&tm_act, act, dims, str, g.nmaxB, g.rmax)) != WR_OK) return st;
   }
   if ((st = set_smem_attr<true>()) != WR_OK) return st;
   if ((st = set_smem_attr<false>()) != WR_OK) return st;
