@@ -656,9 +656,16 @@ struct Work {
 // boundaries); every role of the CTA walks the same sequence.  Tiles are
 // numbered expert-major; inside an expert the token tile varies fastest,
 // then the weight-row tile.
+//
+// gate/up: when the range ends inside a tile, that piece runs first.  The
+// CTA holding a tile's last piece sums the tile's partials (the fixup); run
+// at the end of the range, that sum is the tail of the kernel, run first it
+// overlaps the MMAs of the whole tiles that follow.  The order of pieces
+// changes no sum: partials are added in CTA order.
 template <bool kGU>
 struct WorkIter {
-  int64_t u, u1;
+  int64_t u, u1;    // the piece sequence being walked
+  int64_t u2, u2e;  // then [u2, u2e) (empty when u2 >= u2e)
   int e;
   SplitK sk;
 
@@ -669,11 +676,26 @@ struct WorkIter {
     if (sk.U == 0 || (int)blockIdx.x >= sk.G) return false;
     u = sk.u_lo(blockIdx.x);
     u1 = sk.u_lo(blockIdx.x + 1);
+    u2 = u2e = 0;
+    if (kGU && u < u1 && u1 % sk.kc != 0) {
+      const int64_t lo = ((u1 - 1) / sk.kc) * sk.kc;  // first chunk of the last tile
+      if (lo > u) {  // the end-cut piece [lo, u1) first, then [u, lo)
+        u2 = u;
+        u2e = lo;
+        u = lo;
+      }
+    }
     return u < u1;
   }
 
   WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
-    if (u >= u1) return false;
+    if (u >= u1) {
+      if (u2 >= u2e) return false;
+      u = u2;
+      u1 = u2e;
+      u2 = u2e = 0;
+      e = 0;  // tiles restart below the piece already walked
+    }
     const int tile = (int)(u / sk.kc);
     const int kc0 = (int)(u - (int64_t)tile * sk.kc);
     const int64_t room = u1 - u;
