@@ -63,8 +63,8 @@ constexpr int kWRows = 256;              // MMA N: weight rows per MMA
 constexpr int kRowsA = 128;              // gate/up tile: rows of gate and of up
 constexpr int kRowsB = 256;              // down tile: rows of Wd (= rows of H)
 constexpr int kNMaxA = kTokM;            // tokens per gate/up tile
-constexpr int kNMaxB = 64;               // tokens per down tile, act_hi and act_lo rows stacked
-constexpr int kNMaxBSplit = 128;         // tokens per down tile, act_hi and act_lo as two A tiles
+constexpr int kNMaxB = 64;               // tokens per down accumulator (act_hi, act_lo: 128 A rows)
+constexpr int kNMaxBWide = 128;          // tokens per down tile above 64 tokens: both accumulators
 constexpr int kRowB = kBK * 2;           // bytes of one row per stage
 constexpr int kWBox = 128;               // weight rows per TMA box
 constexpr int kBoxRows = 16;             // token rows: tiles are multiples of this
@@ -75,10 +75,7 @@ constexpr int kGemmThreads = 224;        // 7 warps
 constexpr int kTmemCols = 512;           // two accumulator buffers of 256 columns
 constexpr int kAccStride = 256;          // columns between accumulator buffers
 constexpr int kSmemMax = 232448;         // 227 KB opt-in shared memory per CTA
-constexpr int kStagePitch = 17;          // down epilogue: floats per parked token (16 + pad)
-constexpr int kXchgBytes = kNMaxB * kStagePitch * 4;
 constexpr int kSmemBase = 1024 + 512;    // alignment slack, barriers
-constexpr int kSmemReserve = kSmemBase + kXchgBytes;  // ... and the down epilogue's exchange
 constexpr int kMaxWStages = 8;           // weight ring depth limit
 constexpr int kMaxTStages = 4;           // token ring depth limit
 // barriers (full/empty of both rings, 2 x accumulator full/empty, drain) and
@@ -622,12 +619,12 @@ struct GemmArgs {
   int H, I;
   int nmax;            // token rows per tile
   int kc_total;        // K chunks of kBK per tile (gate/up: over H, down: over I)
-  int rmax;            // rows of one activation half (lo rows start at rmax)
+  int rmax;            // token rows (padded per expert)
   int wstages, tstages;  // weight ring / token ring depth
   int tstage_bytes;      // token slot: gate/up nmax rows, down 2 * nmax rows
-  int hl_split;          // down: act_hi and act_lo are two 128-row A tiles (2 MMAs per step)
+  int wide;              // down, nmax 128: a tile uses both accumulators (tokens 0..63, 64..127)
   const float* row_w;  // gate/up epilogue: per-row routing weight
-  uint16_t* act;       // gate/up output: [2][rmax][I] bf16 (hi, lo)
+  uint16_t* act;       // gate/up output: [2 rmax][I] bf16, rows as act_row_hi / + 16
   float* ypart;        // down output: [jmax][rmax][H] fp32
   int jmax;            // CTAs per tile, at most (gate/up: kJMaxA)
   float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32
@@ -747,6 +744,13 @@ WR_DEVINL uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
   return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
 }
 
+// Activation rows: token row r's act_hi is row act_row_hi(r) and its act_lo
+// 16 rows further: blocks of 16 act_hi rows, each followed by the same 16
+// tokens' act_lo rows.  A down tile's 2n rows are then one TMA box, and as an
+// MMA's A rows they put token t's two halves in accumulator lanes 32q + l and
+// 32q + 16 + l (q = t / 16, l = t % 16): the same warp, 16 lanes apart.
+WR_DEVINL int64_t act_row_hi(int r) { return 2 * (int64_t)(r & ~15) + (r & 15); }
+
 // act = silu(g) * u * wt for 16 consecutive intermediate rows i.. of one
 // token, stored as bf16 hi (act rounded) and lo (act - hi rounded).
 WR_DEVINL void swiglu_store16(const float (&g)[16], const float (&u)[16], float wt, uint16_t* hi,
@@ -781,10 +785,10 @@ WR_DEVINL void swiglu_store16(const float (&g)[16], const float (&u)[16], float 
 // gate/up: B rows 0..127 = gate rows m0.., 128..255 = up rows m0.., so
 //   accumulator lane t (token) holds gate and up of the same rows in columns
 //   c and 128 + c: SwiGLU runs in the thread that owns the token.
-// down:    up to 64 tokens: A rows 0..n-1 = act_hi of the tile's tokens,
-//   rows n_max.. = act_lo, so lanes t and n_max + t hold the two halves of
-//   token t's output; above 64 tokens: act_hi and act_lo are two 128-row A
-//   tiles, two MMAs per K step into the same accumulator.
+// down:    up to 64 tokens per tile; A = the tile's 2n activation rows
+//   (act_hi and act_lo in blocks of 16, see act_row_hi), so lanes 32q + l
+//   and 32q + 16 + l hold the two halves of token 16q + l's output and a
+//   warp shuffle adds them.  One MMA per K step at every token count.
 //
 // Warp roles: 0 weight loads, 6 token loads (one elected lane each), 1 TMEM
 // owner + MMA issue (one elected lane), 2..5 epilogue (TMEM lane quarter
@@ -820,8 +824,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  // down epilogue exchange (stacked act_hi / act_lo only; the host reserves it then)
-  float* xchg = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(fullW) + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -897,11 +899,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_load_3d(s + kWBox * kRowB, &tm_w, kx, kGU ? a.I + w.m0 : w.m0 + kWBox, w.e,
                         &full[st], pol);
           } else {
-            const CUtensorMap* tm = &tm_b.m[nbox - 1];
-            tma_load_2d(s, tm, kx, w.row0, &full[st], pol);
-            if (!kGU)  // act_lo rows at tile rows nmax.. (stacked) or in the second A tile
-              tma_load_2d(s + (a.hl_split ? kTokM : a.nmax) * kRowB, tm, kx, a.rmax + w.row0,
-                          &full[st], pol);
+            // gate/up: the tile's n token rows; down: its 2n activation rows
+            // (act_hi / act_lo blocks of 16, row0 a multiple of 16)
+            if (kGU)
+              tma_load_2d(s, &tm_b.m[nbox - 1], kx, w.row0, &full[st], pol);
+            else {  // at most 128 rows per box: a wide tile's tokens 64.. in a second box
+              const int b0 = nbox < kTokMaps / 2 ? nbox : kTokMaps / 2;
+              tma_load_2d(s, &tm_b.m[2 * b0 - 1], kx, 2 * w.row0, &full[st], pol);
+              if (nbox > b0)
+                tma_load_2d(s + kTokBytes, &tm_b.m[2 * (nbox - b0) - 1], kx,
+                            2 * w.row0 + kTokM, &full[st], pol);
+            }
           }
           ++issued;
           if (++st == stages) {
@@ -924,8 +932,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       it.init(a);
       Work w;
       for (; ok && it.next(a, mv, w); ++j) {
-        const int ab = j & 1;
-        const uint32_t aph = (uint32_t)(j >> 1) & 1u;
+        // two accumulator buffers in turn, or (wide tiles) one of 512 columns
+        const int ab = a.wide ? 0 : (j & 1);
+        const uint32_t aph = a.wide ? (uint32_t)(j & 1) : (uint32_t)(j >> 1) & 1u;
         if (!mbar_wait(&tempty[ab], aph ^ 1u, abort)) {
           if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
           break;
@@ -946,8 +955,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
             const uint64_t wdesc = sw128_desc(sw_addr + kk * 32);
             umma_bf16(d, sw128_desc(st_addr + kk * 32), wdesc, idesc, acc);
-            if (!kGU && a.hl_split)  // act_lo tile into the same accumulator
-              umma_bf16(d, sw128_desc(st_addr + kTokM * kRowB + kk * 32), wdesc, idesc, 1u);
+            if (!kGU && w.n > kNMaxB)  // tokens 64.. (A rows 128..) into the second accumulator
+              umma_bf16(d + kAccStride, sw128_desc(st_addr + kTokBytes + kk * 32), wdesc, idesc,
+                        acc);
           }
           umma_commit(&emptyW[sw]);
           umma_commit(&emptyT[stt]);
@@ -975,8 +985,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     it.init(a);
     Work w;
     for (; it.next(a, mv, w); ++j) {
-      const int ab = j & 1;
-      const uint32_t aph = (uint32_t)(j >> 1) & 1u;
+      const int ab = a.wide ? 0 : (j & 1);
+      const uint32_t aph = a.wide ? (uint32_t)(j & 1) : (uint32_t)(j >> 1) & 1u;
       bool bad = *abort != 0;
       if (!bad && !mbar_wait(&tfull[ab], aph, abort)) {
         if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_ACT);
@@ -993,8 +1003,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool has = 32 * q < w.n;  // warp-uniform: this quarter holds tokens
         const bool live = t < w.n;
         const int r = w.row0 + t;
-        uint16_t* hi = a.act + (int64_t)r * a.I;
-        uint16_t* lo = hi + (int64_t)a.rmax * a.I;
+        uint16_t* hi = a.act + act_row_hi(r) * a.I;
+        uint16_t* lo = hi + 16 * (int64_t)a.I;
         if (w.kc0 == 0 && w.kc1 == a.kc_total) {  // whole tile in this CTA
           if (has) {
             const float wt = live ? __ldg(a.row_w + r) : 0.0f;
@@ -1065,69 +1075,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   u[4 * k] += uv.x; u[4 * k + 1] += uv.y; u[4 * k + 2] += uv.z; u[4 * k + 3] += uv.w;
                 }
               }
-              uint16_t* hrow = a.act + (int64_t)rr * a.I;
-              swiglu_store16(g, u, __ldg(a.row_w + rr), hrow, hrow + (int64_t)a.rmax * a.I,
+              uint16_t* hrow = a.act + act_row_hi(rr) * a.I;
+              swiglu_store16(g, u, __ldg(a.row_w + rr), hrow, hrow + 16 * (int64_t)a.I,
                              w.m0 + c0, a.I);
             }
             if (threadIdx.x == 64) a.cnt[w.tile] = 0;  // ready for the next call
           }
         }
       } else {
-        if (a.hl_split) {
-          // lane t holds token t's whole output (act_hi and act_lo summed by
-          // the MMAs): store 16 consecutive outputs per step.
-          const int t = 32 * q + lane;
-          if (32 * q < w.n) {  // warp-uniform
-            float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + t) * a.H;
-            for (int c0 = 0; c0 < kWRows; c0 += 16) {
-              uint32_t v[16];
-              tmem_ld16(taddr + c0, v);
-              tmem_wait_ld(v);
-              const int h = w.m0 + c0;
-              if (t < w.n) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  if (h + 4 * k < a.H)
-                    *reinterpret_cast<float4*>(yrow + h + 4 * k) =
-                        make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                                    __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
-              }
-            }
-          }
-        } else {
-          // lanes 0..nmax-1: act_hi part of the tile's tokens, lanes nmax..:
-          // act_lo part.  Threads holding a lo part park it in smem; the
-          // thread holding the hi part of the same token adds and stores 16
-          // consecutive outputs.
-          const int L = 32 * q + lane;                  // accumulator lane
-          const bool lo_lane = L >= a.nmax && L < a.nmax + w.n;
-          const bool hi_lane = L < w.n;
-          const bool has = 32 * q < a.nmax + w.n;      // warp-uniform: some lane is used
-          float* park = xchg + (lo_lane ? L - a.nmax : (hi_lane ? L : 0)) * kStagePitch;
-          float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + L) * a.H;
+        // Lane l < 16 of quarter q holds the act_hi part of token 16q + l,
+        // lane l + 16 its act_lo part: one shuffle adds them (the same sum in
+        // both lanes), and each lane stores 8 of every 16 outputs.
+        // A wide tile's tokens 64.. are in the second accumulator, same lanes.
+        for (int acc_i = 0; acc_i * kNMaxB < w.n; ++acc_i) {
+          const int tok = acc_i * kNMaxB + 16 * q + (lane & 15);
+          if (tok - (lane & 15) >= w.n) continue;  // warp-uniform: this quarter holds no tokens
+          const bool live = tok < w.n;
+          const bool upper = lane >= 16;  // stores columns 8..15 of each 16
+          float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + tok) * a.H;
           for (int c0 = 0; c0 < kWRows; c0 += 16) {
             uint32_t v[16];
-            if (has) {
-              tmem_ld16(taddr + c0, v);
-              tmem_wait_ld(v);
-              if (lo_lane) {
+            tmem_ld16(taddr + acc_i * kAccStride + c0, v);
+            tmem_wait_ld(v);
+            float o[8];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) park[c] = __uint_as_float(v[c]);
-              }
+            for (int c = 0; c < 8; ++c) {
+              const float x0 = __uint_as_float(v[c]), x1 = __uint_as_float(v[c + 8]);
+              const float s0 = x0 + __shfl_xor_sync(0xffffffffu, x0, 16);
+              const float s1 = x1 + __shfl_xor_sync(0xffffffffu, x1, 16);
+              o[c] = upper ? s1 : s0;
             }
-            named_bar_sync(1, 128);
-            if (hi_lane) {
-              const int h = w.m0 + c0;
+            const int h = w.m0 + c0 + (upper ? 8 : 0);
+            if (live) {
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
+              for (int k = 0; k < 2; ++k)
                 if (h + 4 * k < a.H)
                   *reinterpret_cast<float4*>(yrow + h + 4 * k) =
-                      make_float4(__uint_as_float(v[4 * k]) + park[4 * k],
-                                  __uint_as_float(v[4 * k + 1]) + park[4 * k + 1],
-                                  __uint_as_float(v[4 * k + 2]) + park[4 * k + 2],
-                                  __uint_as_float(v[4 * k + 3]) + park[4 * k + 3]);
+                      make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
             }
-            named_bar_sync(1, 128);
           }
         }
       }
@@ -1213,7 +1198,6 @@ struct GroupedPlan {
   int kcA, kcB;      // K chunks (over H, over I)
   int wstA, tstA, tbA;  // gate/up rings: weight depth, token depth, token slot bytes
   int wstB, tstB, tbB;  // down rings
-  int hl_split;         // down: act_hi / act_lo as two 128-row A tiles
   int cnt_words;     // gate/up tile counters (>= gate/up tiles)
   int jmaxB;         // down: partial sums per tile, at most
   size_t off_ids, off_w, off_slot, off_meta, off_rtok, off_re, off_rw, off_xg, off_act, off_y,
@@ -1247,17 +1231,16 @@ GroupedPlan make_plan(const Problem& p) {
   const int TK = p.T * p.K;
   const int n16 = (p.T + 15) & ~15;
   g.nmaxA = n16 < kNMaxA ? n16 : kNMaxA;
-  g.hl_split = n16 > kNMaxB;
-  g.nmaxB = g.hl_split ? kNMaxBSplit : n16;
+  g.nmaxB = n16 <= kNMaxB ? n16 : kNMaxBWide;
   g.rmax = (TK + 15 * p.ep_num + 15) & ~15;
   g.mtA = (p.I + kRowsA - 1) / kRowsA;
   g.mtB = (p.H + kRowsB - 1) / kRowsB;
   g.kcA = (p.H + kBK - 1) / kBK;
   g.kcB = (p.I + kBK - 1) / kBK;
   g.tbA = g.nmaxA * kRowB;
-  g.tbB = g.hl_split ? 2 * kTokM * kRowB : 2 * g.nmaxB * kRowB;
+  g.tbB = 2 * g.nmaxB * kRowB;
   ring_split(g.tbA, kSmemBase, &g.wstA, &g.tstA);
-  ring_split(g.tbB, g.hl_split ? kSmemBase : kSmemReserve, &g.wstB, &g.tstB);
+  ring_split(g.tbB, kSmemBase, &g.wstB, &g.tstB);
   size_t o = kWsControlBytes;
   g.off_ids = o; o += a256(4 * (size_t)TK);
   g.off_w = o; o += a256(4 * (size_t)TK);
@@ -1402,7 +1385,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.I, (cuuint64_t)2 * g.rmax};
     const cuuint64_t str[1] = {(cuuint64_t)p.I * 2};
-    if ((st = encode_token_maps(&tm_act, act, dims, str, g.nmaxB, g.rmax)) != WR_OK) return st;
+    if ((st = encode_token_maps(&tm_act, act, dims, str, 2 * g.nmaxB, 2 * g.rmax)) != WR_OK)
+      return st;
   }
   if ((st = set_smem_attr<true>()) != WR_OK) return st;
   if ((st = set_smem_attr<false>()) != WR_OK) return st;
@@ -1420,7 +1404,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.cnt = tcnt;
   ga.status = status;
 
-  ga.hl_split = 0;
+  ga.wide = 0;
   GemmArgs a1 = ga;
   a1.nmax = g.nmaxA;
   a1.kc_total = g.kcA;
@@ -1440,9 +1424,9 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   a2.wstages = g.wstB;
   a2.tstages = g.tstB;
   a2.tstage_bytes = g.tbB;
-  a2.hl_split = g.hl_split;
+  a2.wide = g.nmaxB > kNMaxB;
   const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB +
-                       (g.hl_split ? kSmemBase : kSmemReserve);
+                       kSmemBase;
   ce = launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream, tm_dn,
                   tm_act, a2);
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (down) launch");
