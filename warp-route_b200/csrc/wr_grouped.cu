@@ -87,11 +87,12 @@ constexpr int kJMaxB = 4;                // down: partial sums per output tile, 
 constexpr int kJMaxBLimit = 16;          // ... and at most this one (few tiles: expert parallel)
 
 // Bucket metadata (int32 words in the workspace), written by the bucketing:
-//   [0] rows in use, [1] gate/up tiles, [2] down tiles, and from word 16
-//   cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
-//   preA[E+1], preB[E+1] (tiles before each expert).
+//   [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] down cost, and
+//   from word 16 cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
+//   preA[E+1], preB[E+1] (tiles before each expert), costB[E+1] (down cost
+//   before each expert, see down_chunk_cost).
 constexpr int kMetaHdr = 16;
-__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 6 * E + 2; }
+__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 7 * E + 3; }
 struct MetaView {
   const int* cnt;
   const int* base;
@@ -99,6 +100,7 @@ struct MetaView {
   const int* ntlB;
   const int* preA;
   const int* preB;
+  const int* costB;
 };
 __host__ __device__ inline MetaView meta_view(const int* m, int E) {
   MetaView v;
@@ -108,7 +110,34 @@ __host__ __device__ inline MetaView meta_view(const int* m, int E) {
   v.ntlB = v.ntlA + E;
   v.preA = v.ntlB + E;
   v.preB = v.preA + E + 1;
+  v.costB = v.preB + E + 1;
   return v;
+}
+
+// Down work is split by cost, not by chunk count.  With tiles above 64
+// tokens (both accumulators, two MMAs per K step) a chunk costs 6 units
+// there and 5 elsewhere (measured: such CTAs ran about 1.2x as long per
+// chunk); otherwise every chunk costs 1, which is the plain chunk split.
+constexpr int kCostOne = 5;
+constexpr int kCostWide = 6;
+__host__ __device__ inline int down_chunk_cost(int n, int nmaxB) {
+  return nmaxB > kNMaxB ? (n > kNMaxB ? kCostWide : kCostOne) : 1;
+}
+__host__ __device__ inline int down_cost_max(int nmaxB) { return nmaxB > kNMaxB ? kCostWide : 1; }
+
+// Per-expert down cost: chunk costs of its full and last token tiles and the
+// cost of one H tile row of its token tiles (r).
+struct DownCost {
+  int wfull, wlast;
+  int64_t r;
+};
+__host__ __device__ inline DownCost down_cost_of(int cnt, int nt, int nmaxB, int kc) {
+  DownCost d;
+  const int np = (cnt + 15) & ~15;
+  d.wfull = down_chunk_cost(nmaxB, nmaxB);
+  d.wlast = nt > 0 ? down_chunk_cost(np - (nt - 1) * nmaxB, nmaxB) : 0;
+  d.r = nt > 0 ? (int64_t)kc * ((int64_t)(nt - 1) * d.wfull + d.wlast) : 0;
+  return d;
 }
 
 // ---------------------------------------------------------------------------
@@ -251,15 +280,24 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 struct BucketArgs {
   const int32_t* ids;  // [TK], written by the routing CTAs of the same launch
   const float* w;
-  int TK, K, ep_first, E, nmaxA, nmaxB, mtA, mtB;
+  int TK, K, ep_first, E, nmaxA, nmaxB, mtA, mtB, kcB;
   int* meta;
   int32_t* slot;
   int32_t* row_tok;
-  int2* row_tile;
+  int4* row_tile;  // per row: {cost position of its down tile at H tile 0, cost per H tile, chunk cost}
   float* row_w;
   uint32_t* tile_cnt;
   int cnt_words;
 };
+
+// Row i of expert e: its down tile's cost position at H tile 0, the cost
+// between H tiles, its chunk cost (the combine finds the tile's CTAs so).
+WR_DEVINL int4 down_row_tile(int i, int e, int nmaxB, int kcB, const int* costB, const int* rowB,
+                             const int (*wB)[2], const int* ntlB) {
+  const int tn = i / nmaxB;
+  const int wt = tn == ntlB[e] - 1 ? wB[e][1] : wB[e][0];
+  return make_int4(costB[e] + tn * kcB * wB[e][0], rowB[e], wt, 0);
+}
 
 // Run by one whole CTA.  s_ids: dynamic shared memory of 8 * TK bytes when
 // TK <= kBucketSmemIds (the ids, then the weights, are staged there).  The
@@ -268,17 +306,19 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
   const int32_t* __restrict__ ids = b.ids;
   const float* __restrict__ w = b.w;
   const int TK = b.TK, K = b.K, ep_first = b.ep_first, E = b.E;
-  const int nmaxA = b.nmaxA, nmaxB = b.nmaxB, mtA = b.mtA, mtB = b.mtB;
+  const int nmaxA = b.nmaxA, nmaxB = b.nmaxB, mtA = b.mtA, mtB = b.mtB, kcB = b.kcB;
   int* __restrict__ meta = b.meta;
   int32_t* __restrict__ slot = b.slot;
   int32_t* __restrict__ row_tok = b.row_tok;
-  int2* __restrict__ row_tile = b.row_tile;
+  int4* __restrict__ row_tile = b.row_tile;
   float* __restrict__ row_w = b.row_w;
   uint32_t* __restrict__ tile_cnt = b.tile_cnt;
   const int cnt_words = b.cnt_words;
   __shared__ int s_cnt[kMaxExperts];
   __shared__ int s_base[kMaxExperts];
-  __shared__ int s_preB[kMaxExperts];
+  __shared__ int s_costB[kMaxExperts];  // down cost before the expert
+  __shared__ int s_rowB[kMaxExperts];   // down cost of one H tile row of its token tiles
+  __shared__ int s_wB[kMaxExperts][2];  // chunk cost: full token tiles, last token tile
   __shared__ int s_ntlB[kMaxExperts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const bool staged = TK <= kBucketSmemIds;
@@ -323,7 +363,8 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     int* ntlB = ntlA + E;
     int* preA = ntlB + E;
     int* preB = preA + E + 1;
-    int b = 0, pa = 0, pb = 0;
+    int* costB = preB + E + 1;
+    int b = 0, pa = 0, pb = 0, cb = 0;
     for (int e = 0; e < E; ++e) {
       const int n = s_cnt[e];
       const int np = (n + 15) & ~15;
@@ -337,16 +378,24 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
       s_ntlB[e] = nb;
       preA[e] = pa;
       preB[e] = pb;
-      s_preB[e] = pb;
+      const DownCost dc = down_cost_of(n, nb, nmaxB, kcB);
+      costB[e] = cb;
+      s_costB[e] = cb;
+      s_rowB[e] = (int)dc.r;
+      s_wB[e][0] = dc.wfull;
+      s_wB[e][1] = dc.wlast;
       b += np;
       pa += mtA * na;
       pb += mtB * nb;
+      cb += mtB * (int)dc.r;
     }
     preA[E] = pa;
     preB[E] = pb;
+    costB[E] = cb;
     meta[0] = b;
     meta[1] = pa;
     meta[2] = pb;
+    meta[3] = cb;
   }
   __syncthreads();
   for (int e = warp; e < E; e += nw) {
@@ -359,7 +408,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
         const int r = run + __popc(bal & ((1u << lane) - 1u));
         slot[j + lane] = r;
         row_tok[r] = (j + lane) / K;
-        row_tile[r] = make_int2(s_preB[e] + (r - b0) / nmaxB, s_ntlB[e]);
+        row_tile[r] = down_row_tile(r - b0, e, nmaxB, kcB, s_costB, s_rowB, s_wB, s_ntlB);
         row_w[r] = sw[j + lane];
       }
       run += __popc(bal);
@@ -367,7 +416,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     const int end = b0 + ((s_cnt[e] + 15) & ~15);
     for (int r = run + lane; r < end; r += 32) {
       row_tok[r] = -1;
-      row_tile[r] = make_int2(s_preB[e] + (r - b0) / nmaxB, s_ntlB[e]);
+      row_tile[r] = down_row_tile(r - b0, e, nmaxB, kcB, s_costB, s_rowB, s_wB, s_ntlB);
       row_w[r] = 0.0f;
     }
   }
@@ -479,29 +528,52 @@ WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid, int jmax) {
   return s;
 }
 
+// The down split: chunks laid end to end as in SplitK, chunk (tile, k) at
+// cost position pos(tile) + k * w(tile); CTA c takes the chunks whose
+// position lies in [c C / G, (c + 1) C / G).  With all costs 1 this is
+// SplitK.  The grid cap keeps each range >= L chunks of the dearest kind,
+// so a tile still spans at most jmax CTAs.
+struct CostSplit {
+  int64_t C;  // total cost
+  int G;
+  WR_DEVINL int cta_of(int64_t p) const { return (int)(((p + 1) * G - 1) / C); }
+  WR_DEVINL int64_t lo(int c) const { return (int64_t)c * C / G; }
+};
+
+WR_DEVINL CostSplit make_costsplit(int64_t C, int kc, int grid, int jmax, int wmax) {
+  CostSplit s;
+  s.C = C;
+  const int64_t L = (kc + jmax - 2) / (jmax - 1);
+  int64_t g = C / (L * wmax);
+  if (g < 1) g = 1;
+  if (g > grid) g = grid;
+  s.G = (int)g;
+  return s;
+}
+
 // out[t, :] = sum over k ascending of (slot >= 0 ? sum over the tile's
 // partials in slot order : 0).  One fixed order: deterministic.
 __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypart,
                                                  const int32_t* __restrict__ slot,
-                                                 const int2* __restrict__ row_tile,
+                                                 const int4* __restrict__ row_tile,
                                                  const int* __restrict__ meta, int K, int H4,
-                                                 int rmax, int kcB, int grid, int jmax,
+                                                 int rmax, int kcB, int grid, int jmax, int wmax,
                                                  float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
-  const SplitK sk = make_splitk(meta[2], kcB, grid, jmax);
+  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, wmax);
   const int mt = (h * 4) / kRowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
     const int r = slot[(int64_t)t * K + k];
     if (r < 0) continue;
-    const int2 rt = row_tile[r];
-    const int tile = rt.x + mt * rt.y;
-    const int c0 = sk.first_cta(tile);
-    const int c1 = sk.last_cta(tile);
+    const int4 rt = row_tile[r];
+    const int64_t pos = rt.x + (int64_t)mt * rt.y;
+    const int c0 = cs.cta_of(pos);
+    const int c1 = cs.cta_of(pos + (int64_t)(kcB - 1) * rt.z);
     for (int j = 0; j <= c1 - c0; ++j) {
       const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h];
       acc.x += v.x;
@@ -527,9 +599,10 @@ constexpr int kCtlExit = 1;  // control word: CTAs done (the streaming kernel's,
 
 __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ ypart,
                                                     const int32_t* __restrict__ slot,
-                                                    const int2* __restrict__ row_tile,
+                                                    const int4* __restrict__ row_tile,
                                                     const int* __restrict__ meta, int K, int H,
-                                                    int rmax, int kcB, int grid, int jmax, int t0,
+                                                    int rmax, int kcB, int grid, int jmax,
+                                                    int wmax, int t0,
                                                     int Tc, const CommView comm,
                                                     uint32_t* __restrict__ ctl,
                                                     float* __restrict__ out) {
@@ -539,7 +612,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
   if (threadIdx.x == 0) s_ep = *comm.epoch + 1;
   __syncthreads();
   const uint32_t ep = s_ep;
-  const SplitK sk = make_splitk(meta[2], kcB, grid, jmax);
+  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, wmax);
   const int H4 = H / 4;
   const int items = Tc * H4;
   const int stride = gridDim.x * blockDim.x;
@@ -552,9 +625,9 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
     for (int k = 0; k < K; ++k) {
       const int r = slot[(int64_t)t * K + k];
       if (r < 0) continue;
-      const int2 rt = row_tile[r];
-      const int tile = rt.x + mt * rt.y;
-      const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
+      const int4 rt = row_tile[r];
+      const int64_t pos = rt.x + (int64_t)mt * rt.y;
+      const int c0 = cs.cta_of(pos), c1 = cs.cta_of(pos + (int64_t)(kcB - 1) * rt.z);
       for (int j = 0; j <= c1 - c0; ++j) {
         const float4 v = ypart[((int64_t)j * rmax + r) * H4 + h4];
         acc.x += v.x;
@@ -715,6 +788,79 @@ struct WorkIter {
     w.n = min(a.nmax, np - tn * a.nmax);
     w.rot = (int)(((unsigned)tile * 37u) % (unsigned)len);
     return true;
+  }
+};
+
+// The down GEMM's sequence: the pieces of the tiles whose chunks' cost
+// positions lie in this CTA's range (CostSplit), in tile order.
+template <>
+struct WorkIter<false> {
+  CostSplit cs;
+  SplitK sk;  // not used by the down GEMM (the gate/up fixup's)
+  int64_t p, p1;  // next chunk position to take, end of the range
+  int e, m, tn;   // the tile p lies in (or the next one)
+
+  WR_DEVINL bool init(const GemmArgs& a) {
+    const int64_t C = __ldg(a.meta + 3);
+    cs = make_costsplit(C, a.kc_total, gridDim.x, a.jmax, down_cost_max(a.nmax));
+    if (C == 0 || (int)blockIdx.x >= cs.G) return false;
+    p = cs.lo(blockIdx.x);
+    p1 = cs.lo(blockIdx.x + 1);
+    if (p >= p1) return false;
+    const MetaView mv = meta_view(a.meta, a.E);
+    e = 0;
+    while (e + 1 < a.E && __ldg(mv.costB + e + 1) <= p) ++e;  // experts without tiles cost 0
+    const int nt = __ldg(mv.ntlB + e);
+    const DownCost dc = down_cost_of(__ldg(mv.cnt + e), nt, a.nmax, a.kc_total);
+    const int64_t rel = p - __ldg(mv.costB + e);
+    m = (int)(rel / dc.r);
+    tn = (int)((rel - (int64_t)m * dc.r) / ((int64_t)a.kc_total * dc.wfull));
+    if (tn > nt - 1) tn = nt - 1;
+    return true;
+  }
+
+  WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
+    const int kc = a.kc_total;
+    const int mt = (a.H + kRowsB - 1) / kRowsB;
+    while (p < p1 && e < a.E) {
+      const int nt = __ldg(mv.ntlB + e);
+      const int cnt = __ldg(mv.cnt + e);
+      const DownCost dc = down_cost_of(cnt, nt, a.nmax, kc);
+      const int wt = tn == nt - 1 ? dc.wlast : dc.wfull;
+      const int64_t pos =
+          __ldg(mv.costB + e) + (int64_t)m * dc.r + (int64_t)tn * kc * dc.wfull;
+      const int64_t k0 = p > pos ? (p - pos + wt - 1) / wt : 0;
+      int64_t k1 = (p1 - pos + wt - 1) / wt;
+      if (k1 > kc) k1 = kc;
+      const int ce = e, cm = m, ctn = tn;
+      if (++tn == nt) {  // the tile after this one
+        tn = 0;
+        if (++m == mt) {
+          m = 0;
+          do {
+            ++e;
+          } while (e < a.E && __ldg(mv.ntlB + e) == 0);
+        }
+      }
+      if (k0 >= kc) continue;  // p is past this tile's last chunk
+      if (k1 <= k0) {
+        p = p1;
+        return false;
+      }
+      p = pos + k1 * wt;
+      w.tile = __ldg(mv.preB + ce) + cm * nt + ctn;
+      w.kc0 = (int)k0;
+      w.kc1 = (int)k1;
+      w.j = (int)blockIdx.x - cs.cta_of(pos);
+      w.e = ce;
+      w.m0 = cm * kRowsB;
+      const int np = (cnt + 15) & ~15;
+      w.row0 = __ldg(mv.base + ce) + ctn * a.nmax;
+      w.n = min(a.nmax, np - ctn * a.nmax);
+      w.rot = (int)(((unsigned)w.tile * 37u) % (unsigned)(k1 - k0));
+      return true;
+    }
+    return false;
   }
 };
 
@@ -1247,7 +1393,7 @@ GroupedPlan make_plan(const Problem& p) {
   g.off_slot = o; o += a256(4 * (size_t)TK);
   g.off_meta = o; o += a256(4 * (size_t)meta_words(p.ep_num));
   g.off_rtok = o; o += a256(4 * (size_t)g.rmax);
-  g.off_re = o; o += a256(8 * (size_t)g.rmax);
+  g.off_re = o; o += a256(16 * (size_t)g.rmax);
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
   g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
@@ -1318,7 +1464,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   int32_t* slot = reinterpret_cast<int32_t*>(wsb + g.off_slot);
   int* meta = reinterpret_cast<int*>(wsb + g.off_meta);
   int32_t* rtok = reinterpret_cast<int32_t*>(wsb + g.off_rtok);
-  int2* rtile = reinterpret_cast<int2*>(wsb + g.off_re);
+  int4* rtile = reinterpret_cast<int4*>(wsb + g.off_re);
   float* rw = reinterpret_cast<float*>(wsb + g.off_rw);
   uint16_t* xg = reinterpret_cast<uint16_t*>(wsb + g.off_xg);
   uint16_t* act = reinterpret_cast<uint16_t*>(wsb + g.off_act);
@@ -1341,6 +1487,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ba.nmaxB = g.nmaxB;
   ba.mtA = g.mtA;
   ba.mtB = g.mtB;
+  ba.kcB = g.kcB;
   ba.meta = meta;
   ba.slot = slot;
   ba.row_tok = rtok;
@@ -1440,16 +1587,17 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
       if (blocks > 4 * sms) blocks = 4 * sms;
       ce = launch_pdl(k_combine_ar, dim3(blocks), dim3(256), 0, stream,
                       reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                      (const int2*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
-                      g.jmaxB, t0, Tc, *comm, reinterpret_cast<uint32_t*>(ws), out);
+                      (const int4*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
+                      g.jmaxB, down_cost_max(g.nmaxB), t0, Tc, *comm,
+                      reinterpret_cast<uint32_t*>(ws), out);
       if (ce != cudaSuccess) return cuda_fail(ce, "combine (all-reduce) launch");
     }
     return WR_OK;
   }
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                  (const int2*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
-                  reinterpret_cast<float4*>(out));
+                  (const int4*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
+                  down_cost_max(g.nmaxB), reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 
