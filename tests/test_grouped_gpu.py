@@ -200,3 +200,29 @@ def test_many_pairs_bucket_reads_global():
     out, ids, w = _run(L, E, H, I, K)
     _check_routing(ids, w, L, K)
     _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, 1, 357, 719], L.router_bias)
+
+
+@pytest.mark.parametrize("T", [6, 100])
+def test_one_rank_allreduce_combine_matches_plain_combine(T):
+    """The all-reducing combine step (one launch per 64 tokens), given a
+    one-rank communicator, sums a single partial output and must equal the
+    plain combine.  At T = 100 every token picks the same first expert, so
+    its 100 rows form a tile above 64 tokens (both accumulators, the
+    cost-weighted down split) and the step runs as two launches."""
+    from warp_route import functional as F
+    E, H, I, K = 8, 1024, 2048, 2
+    L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=67, tokens=T)
+    bias = torch.zeros(E, dtype=torch.float32, device="cuda")
+    bias[3] = 50.0
+    ref = F.fused_moe_routed(L.x, L.gate_w, L.weight_buf, E, H, I, K, router_bias=bias)[0]
+    _C = F._load_extension()
+    comm = _C.comm_create(0, 1, H)
+    try:
+        for _ in range(2):  # the second call runs under the next epoch
+            got = _C.fused_moe_allreduce(L.x, L.gate_w, L.weight_buf, E, H, I, K, comm, bias,
+                                         0, 0)[0]
+            torch.cuda.synchronize()
+            assert oracle.rel_l2(got.cpu().numpy(), ref.cpu().numpy()) <= 1e-6
+    finally:
+        _C.comm_destroy(comm)
+    _check_rows(ref, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, T - 1], bias)
