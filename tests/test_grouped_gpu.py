@@ -125,15 +125,23 @@ def test_edge_shapes(E, H, I, K, T):
     _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, list(range(T)))
 
 
-def test_expert_parallel_shards_sum_to_full():
-    E, H, I, K, T = 8, 1024, 2048, 2, 64
+@pytest.mark.parametrize("T,hot", [(64, False), (130, True)])
+def test_expert_parallel_shards_sum_to_full(T, hot):
+    """Four expert shards sum to the whole layer.  With `hot`, a bias sends
+    every token to expert 1 first: shard 0 then holds a tile above 64 tokens
+    (both accumulators, cost-weighted down split) beside small ones."""
+    E, H, I, K = 8, 1024, 2048, 2
+    bias = None
+    if hot:
+        bias = torch.zeros(E, dtype=torch.float32, device="cuda")
+        bias[1] = 50.0
     full = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=17, tokens=T)
-    ref, _, _ = _run(full, E, H, I, K)
+    ref, _, _ = abi_layer(full.x, full.gate_w, full.weight_buf, E, H, I, K, bias=bias)
     acc = torch.zeros_like(ref)
     for r in range(4):
         sh = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=17, tokens=T,
                                   ep_rank=r, ep_size=4)
-        out, _, _ = abi_layer(sh.x, sh.gate_w, sh.weight_buf, E, H, I, K,
+        out, _, _ = abi_layer(sh.x, sh.gate_w, sh.weight_buf, E, H, I, K, bias=bias,
                               ep_first=sh.ep_first, ep_num=sh.ep_num)
         acc += out
     torch.cuda.synchronize()
