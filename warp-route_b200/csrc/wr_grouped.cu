@@ -440,6 +440,14 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_bucket(
   __shared__ int tids[kMaxExperts];
   __shared__ float tws[kMaxExperts];
   __shared__ int s_last;
+  // While the previous kernel finishes: this CTA's share of the router rows
+  // and its token row into L2 (aligned inputs only).  gate_w does not depend
+  // on that kernel and x may, but a prefetch into L2, the point of
+  // coherence, cannot make a later read return stale data.
+  if (threadIdx.x == 0 && vec_ok) {
+    prefetch_share_l2(gate_w, (int64_t)E_all * H * 2, blockIdx.x, gridDim.x);
+    prefetch_share_l2(x + (int64_t)blockIdx.x * H, (int64_t)H * 2, 0, 1);
+  }
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
