@@ -17,12 +17,13 @@
 //                   tile = (expert, 128 intermediate rows, <= 128 tokens):
 //                   D[token, 256] = X_g rows x [128 gate rows; 128 up rows],
 //                   epilogue act = silu(g) * u * w(token, k) stored as bf16
-//                   hi + lo (~16 mantissa bits for the second GEMM)
+//                   hi + lo (~16 mantissa bits for the second GEMM), in
+//                   blocks of 16 act_hi rows each followed by their act_lo
 //   k_grouped_gemm<down>
 //                   tile = (expert, 256 rows of H, <= 64 / 128 tokens):
-//                   D[token, 256] = [act_hi; act_lo] x Wd rows (hi and lo
-//                   stacked in one 128-row A tile, or two A tiles above 64
-//                   tokens), fp32 partials per K split
+//                   D[token half, 256] = act rows x Wd rows, 64 tokens (their
+//                   hi and lo rows: 128 A rows) per accumulator, hi + lo
+//                   added by a warp shuffle; fp32 partials per K split
 //   k_combine       out[t] = sum over k (ascending) of the partials of its
 //   (k_combine_ar)  rows (in CTA order): deterministic; with a communicator
 //                   the ranks' outputs are also summed over NVLink peer
@@ -39,8 +40,9 @@
 // tcgen05.commit to release smem stages and to hand accumulators to the
 // epilogue); warps 2-5 read the accumulators back with tcgen05.ld (warp w
 // reads TMEM lanes 32*(w%4)..+31) and store the results.  Two accumulator
-// buffers let the epilogue of one tile overlap the MMAs of the next.  The
-// K chunks of all tiles are dealt to the CTAs in equal ranges (stream-K).
+// buffers let the epilogue of one tile overlap the MMAs of the next (down
+// tiles above 64 tokens use both).  The K chunks of all tiles are dealt to
+// the CTAs in equal ranges (stream-K; the down GEMM's weighted by cost).
 // No TMA multicast anywhere; every wait is bounded and a wait that runs out
 // sets the workspace status word and winds the CTA down (copies in flight
 // drained, MMAs completed, TMEM freed).
@@ -900,9 +902,10 @@ WR_DEVINL uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
 
 // Activation rows: token row r's act_hi is row act_row_hi(r) and its act_lo
 // 16 rows further: blocks of 16 act_hi rows, each followed by the same 16
-// tokens' act_lo rows.  A down tile's 2n rows are then one TMA box, and as an
-// MMA's A rows they put token t's two halves in accumulator lanes 32q + l and
-// 32q + 16 + l (q = t / 16, l = t % 16): the same warp, 16 lanes apart.
+// tokens' act_lo rows.  A down tile's 2n rows are then one TMA box per 64
+// tokens, and as an MMA's A rows they put token t's two halves (t < 64) in
+// accumulator lanes 32q + l and 32q + 16 + l (q = t / 16, l = t % 16): the
+// same warp, 16 lanes apart.
 WR_DEVINL int64_t act_row_hi(int r) { return 2 * (int64_t)(r & ~15) + (r & 15); }
 
 // act = silu(g) * u * wt for 16 consecutive intermediate rows i.. of one
