@@ -89,8 +89,8 @@ constexpr int kJMaxB = 4;                // down: partial sums per output tile, 
 constexpr int kJMaxBLimit = 16;          // ... and at most this one (few tiles: expert parallel)
 
 // Bucket metadata (int32 words in the workspace), written by the bucketing:
-//   [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] down cost, and
-//   from word 16 cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
+//   [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] down cost, [4]
+//   the largest down chunk cost present, and from word 16 cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
 //   preA[E+1], preB[E+1] (tiles before each expert), costB[E+1] (down cost
 //   before each expert, see down_chunk_cost).
 constexpr int kMetaHdr = 16;
@@ -125,7 +125,6 @@ constexpr int kCostWide = 6;
 __host__ __device__ inline int down_chunk_cost(int n, int nmaxB) {
   return nmaxB > kNMaxB ? (n > kNMaxB ? kCostWide : kCostOne) : 1;
 }
-__host__ __device__ inline int down_cost_max(int nmaxB) { return nmaxB > kNMaxB ? kCostWide : 1; }
 
 // Per-expert down cost: chunk costs of its full and last token tiles and the
 // cost of one H tile row of its token tiles (r).
@@ -366,7 +365,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     int* preA = ntlB + E;
     int* preB = preA + E + 1;
     int* costB = preB + E + 1;
-    int b = 0, pa = 0, pb = 0, cb = 0;
+    int b = 0, pa = 0, pb = 0, cb = 0, wmax = 1;
     for (int e = 0; e < E; ++e) {
       const int n = s_cnt[e];
       const int np = (n + 15) & ~15;
@@ -390,6 +389,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
       pa += mtA * na;
       pb += mtB * nb;
       cb += mtB * (int)dc.r;
+      if (nb > 0) wmax = max(wmax, nb > 1 ? dc.wfull : dc.wlast);
     }
     preA[E] = pa;
     preB[E] = pb;
@@ -398,6 +398,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     meta[1] = pa;
     meta[2] = pb;
     meta[3] = cb;
+    meta[4] = wmax;
   }
   __syncthreads();
   for (int e = warp; e < E; e += nw) {
@@ -567,14 +568,14 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
                                                  const int32_t* __restrict__ slot,
                                                  const int4* __restrict__ row_tile,
                                                  const int* __restrict__ meta, int K, int H4,
-                                                 int rmax, int kcB, int grid, int jmax, int wmax,
+                                                 int rmax, int kcB, int grid, int jmax,
                                                  float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
-  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, wmax);
+  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, meta[4]);
   const int mt = (h * 4) / kRowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
                                                     const int4* __restrict__ row_tile,
                                                     const int* __restrict__ meta, int K, int H,
                                                     int rmax, int kcB, int grid, int jmax,
-                                                    int wmax, int t0,
+                                                    int t0,
                                                     int Tc, const CommView comm,
                                                     uint32_t* __restrict__ ctl,
                                                     float* __restrict__ out) {
@@ -622,7 +623,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
   if (threadIdx.x == 0) s_ep = *comm.epoch + 1;
   __syncthreads();
   const uint32_t ep = s_ep;
-  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, wmax);
+  const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, meta[4]);
   const int H4 = H / 4;
   const int items = Tc * H4;
   const int stride = gridDim.x * blockDim.x;
@@ -802,7 +803,8 @@ struct WorkIter {
 };
 
 // The down GEMM's sequence: the pieces of the tiles whose chunks' cost
-// positions lie in this CTA's range (CostSplit), in tile order.
+// positions lie in this CTA's range (CostSplit), in tile order.  The grid
+// cap uses the largest chunk cost present (meta[4]), as the combine does.
 template <>
 struct WorkIter<false> {
   CostSplit cs;
@@ -812,7 +814,7 @@ struct WorkIter<false> {
 
   WR_DEVINL bool init(const GemmArgs& a) {
     const int64_t C = __ldg(a.meta + 3);
-    cs = make_costsplit(C, a.kc_total, gridDim.x, a.jmax, down_cost_max(a.nmax));
+    cs = make_costsplit(C, a.kc_total, gridDim.x, a.jmax, __ldg(a.meta + 4));
     if (C == 0 || (int)blockIdx.x >= cs.G) return false;
     p = cs.lo(blockIdx.x);
     p1 = cs.lo(blockIdx.x + 1);
@@ -1599,7 +1601,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
       ce = launch_pdl(k_combine_ar, dim3(blocks), dim3(256), 0, stream,
                       reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
                       (const int4*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
-                      g.jmaxB, down_cost_max(g.nmaxB), t0, Tc, *comm,
+                      g.jmaxB, t0, Tc, *comm,
                       reinterpret_cast<uint32_t*>(ws), out);
       if (ce != cudaSuccess) return cuda_fail(ce, "combine (all-reduce) launch");
     }
@@ -1608,7 +1610,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
                   (const int4*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
-                  down_cost_max(g.nmaxB), reinterpret_cast<float4*>(out));
+                  reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 
