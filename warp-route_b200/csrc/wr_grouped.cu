@@ -1220,18 +1220,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int tt = item / (kRowsA / 16);
               const int c0 = (item % (kRowsA / 16)) * 16;
               const int rr = w.row0 + tt;
+              // All partials' loads in flight at once (at most kJMaxA CTAs
+              // share a tile), then the adds in CTA order.
+              float4 gv[kJMaxA][4], uv[kJMaxA][4];
+#pragma unroll
+              for (int cc = 0; cc < kJMaxA; ++cc) {
+                if (cf + cc <= cl) {
+                  const float* src = a.pbuf + (((size_t)(cf + cc) * 2 +
+                                                sk.part_slot(cf + cc, w.tile)) * a.nmax + tt) *
+                                                  kWRows;
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    gv[cc][k] = __ldcg(reinterpret_cast<const float4*>(src + c0) + k);
+                    uv[cc][k] = __ldcg(reinterpret_cast<const float4*>(src + kRowsA + c0) + k);
+                  }
+                }
+              }
               float g[16], u[16];
 #pragma unroll
               for (int c = 0; c < 16; ++c) g[c] = u[c] = 0.0f;
-              for (int c = cf; c <= cl; ++c) {
-                const float* src =
-                    a.pbuf + (((size_t)c * 2 + sk.part_slot(c, w.tile)) * a.nmax + tt) * kWRows;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float4 gv = __ldcg(reinterpret_cast<const float4*>(src + c0) + k);
-                  const float4 uv = __ldcg(reinterpret_cast<const float4*>(src + kRowsA + c0) + k);
-                  g[4 * k] += gv.x; g[4 * k + 1] += gv.y; g[4 * k + 2] += gv.z; g[4 * k + 3] += gv.w;
-                  u[4 * k] += uv.x; u[4 * k + 1] += uv.y; u[4 * k + 2] += uv.z; u[4 * k + 3] += uv.w;
+              for (int cc = 0; cc < kJMaxA; ++cc) {
+                if (cf + cc <= cl) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    g[4 * k] += gv[cc][k].x; g[4 * k + 1] += gv[cc][k].y;
+                    g[4 * k + 2] += gv[cc][k].z; g[4 * k + 3] += gv[cc][k].w;
+                    u[4 * k] += uv[cc][k].x; u[4 * k + 1] += uv[cc][k].y;
+                    u[4 * k + 2] += uv[cc][k].z; u[4 * k + 3] += uv[cc][k].w;
+                  }
                 }
               }
               uint16_t* hrow = a.act + act_row_hi(rr) * a.I;
