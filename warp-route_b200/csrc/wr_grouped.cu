@@ -512,6 +512,9 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
 // and the last CTA to finish the tile adds them (in CTA order) and applies
 // SwiGLU.  G is capped so that every range holds at least
 // ceil(kc / (jmax - 1)) chunks, which bounds the CTAs per tile by jmax.
+// SplitK is the gate/up split; the down GEMM cuts ranges of equal cost
+// instead (CostSplit below), which is the same split when every chunk
+// costs the same.
 // ---------------------------------------------------------------------------
 struct SplitK {
   int64_t U;  // chunks in total
