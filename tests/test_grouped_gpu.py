@@ -234,3 +234,20 @@ def test_one_rank_allreduce_combine_matches_plain_combine(T):
     finally:
         _C.comm_destroy(comm)
     _check_rows(ref, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, T - 1], bias)
+
+
+def test_expert_shard_without_pairs_writes_zeros():
+    """An expert-parallel shard that no token picks (a bias makes experts 0
+    and 1 everyone's choice; this rank holds experts 6-7): no tiles at all,
+    and the output is exactly zero."""
+    E, H, I, K, T = 8, 1024, 2048, 2, 6
+    bias = torch.zeros(E, dtype=torch.float32, device="cuda")
+    bias[0] = bias[1] = 50.0
+    sh = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=71, tokens=T,
+                              ep_rank=3, ep_size=4)
+    for _ in range(2):
+        out, ids, _ = abi_layer(sh.x, sh.gate_w, sh.weight_buf, E, H, I, K, bias=bias,
+                                ep_first=sh.ep_first, ep_num=sh.ep_num)
+        torch.cuda.synchronize()
+        assert set(ids.view(-1).tolist()) == {0, 1}
+        assert torch.equal(out, torch.zeros_like(out))
