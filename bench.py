@@ -1,7 +1,7 @@
 """Benchmark: µs per fused MoE layer and achieved HBM GB/s (decode, bs=1).
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--config mixtral|deepseek|dbrx|tiny]
-                [--parallel tp|ep] [--impl ours|reference]
+                [--parallel tp|ep] [--impl ours|reference] [--extra-configs deepseek,dbrx]
 
 One step = one MoE layer forward for one decode token (router -> top-K ->
 SwiGLU over the selected experts -> weighted combine; plus the hidden-sized
@@ -12,14 +12,20 @@ so every step streams weights from HBM (each step reads more than L2 holds).
 
 Rank 0 prints one JSON line.  `value` is µs per layer (max over ranks, CUDA
 events on the launching stream; the timed steps replay a CUDA graph of the
-layer calls); `e2e` is the same through the public API with the token copied
-in from pinned host memory and the output copied back every step (copies on
-their own streams, overlapping the kernels; the steps replayed from CUDA
-graphs of 64 steps, or eagerly with --no-graph); `roofline` relates
-the fused kernel's algorithmic bytes to the
-measured HBM copy bandwidth; `cpu_baseline` times warp-route's own CPU
-composition (restated in oracle/torch_composition.py) on a bounded sample.
-`--impl reference` times that CPU composition alone, as the reference arm.
+layer calls; at N > 1 every rank's region starts behind a device-side
+rendezvous, so host skew between ranks is not charged to it); `e2e` is the
+same through the public API with the token copied in from pinned host memory
+and the output copied back every step (copies on their own streams,
+overlapping the kernels; the steps replayed from CUDA graphs of 64 steps, or
+eagerly with --no-graph); `roofline` relates the fused kernel's algorithmic
+bytes to the measured HBM copy bandwidth; `parity` checks a sampled layer,
+run through the timed path, against warp-route's CPU composition (and, at
+N > 1, against the whole layer on rank 0's GPU, plus bit-identity across the
+ranks); `cpu_baseline` times that CPU composition (restated in
+oracle/torch_composition.py) on a bounded sample.  `other_configs` carries the
+same measurement for the DeepSeek- and DBRX-shaped layers (expert parallel at
+N > 1).  `--impl reference` times the CPU composition alone, as the reference
+arm.
 
 The line also carries `batched_sweep`: the batched-decode sweep on
 the Mixtral shape (tokens 1, 4, 16, 64, 256; router bias N(0,1) per expert to
@@ -82,6 +88,9 @@ def parse():
     ap.add_argument("--sweep-fused-allreduce", action="store_true",
                     help="N > 1: sum the sweep's batch outputs in the layer's combine step "
                          "over NVLink peer memory instead of NCCL (needs --allreduce fused)")
+    ap.add_argument("--extra-configs", default="deepseek,dbrx",
+                    help="other BASELINE configurations measured in the same run (expert "
+                         "parallel at N > 1), reported under other_configs; empty: none")
     ap.add_argument("--only-sweep", action="store_true",
                     help="run only the batched-decode sweep (N = 1) and print its JSON line")
     return ap.parse_args()
@@ -179,32 +188,46 @@ def dist_setup(args):
 
 
 # ---------------------------------------------------------------------------
-# CPU composition (warp-route's own CPU path, restated in oracle/)
+# CPU composition (warp-route's own CPU path, restated in oracle/): the CPU
+# baseline, the reference arm and the parity checker of the bench line
 # ---------------------------------------------------------------------------
-def cpu_composition_timing(x, gate_w, weight_buf, E, H, I, K, budget_s, max_calls=None,
-                           bias=None):
-    """Time the restated torch_moe_reference on host threads.  Weights are the
-    same layer's selected experts, widened to fp32 (warp-route's own dtype)."""
+def _composition():
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import torch_composition as tc
+    return tc
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    xh = x.detach().float().cpu()
-    gwh = gate_w.detach().float().cpu()
-    bh = None if bias is None else bias.detach().float().cpu()
-    probs = torch.softmax(gwh @ xh + (bh if bh is not None else 0), dim=0)
-    sel = torch.topk(probs, K).indices.tolist()
+
+def _host_experts(weight_buf, E, H, I, sel, dtype):
+    """Host copies (in `dtype`) of the selected experts' [gate, up, down]."""
     elt = weight_buf.element_size()
     stride = ((3 * H * I * elt + 127) // 128 * 128) // elt
     n = I * H
     gate, up, down = [None] * E, [None] * E, [None] * E
     for e in sel:
-        blk = weight_buf[e * stride:e * stride + 3 * n].float().cpu()
+        blk = weight_buf[e * stride:e * stride + 3 * n].to(dtype).cpu()
         gate[e] = blk[:n].view(I, H)
         up[e] = blk[n:2 * n].view(I, H)
         down[e] = blk[2 * n:].view(H, I)
-    for _ in range(3):
+    return gate, up, down
+
+
+def cpu_composition_timing(x, gate_w, weight_buf, E, H, I, K, budget_s, max_calls=None,
+                           bias=None, threads=None, dtype=torch.float32, warmup=3):
+    """Time the restated torch_moe_reference on host threads: median µs per
+    single-token forward over a bounded sample (at most `budget_s` seconds or
+    `max_calls` calls, after `warmup` untimed calls).  Weights are the same
+    layer's selected experts in `dtype` (float32 is warp-route's own dtype;
+    the layer's bf16 values widen exactly).  Returns (µs, calls, threads)."""
+    tc = _composition()
+    threads = threads or (os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    xh = x.detach().to(dtype).cpu()
+    gwh = gate_w.detach().to(dtype).cpu()
+    bh = None if bias is None else bias.detach().float().cpu()
+    probs = torch.softmax(gwh.float() @ xh.float() + (bh if bh is not None else 0), dim=0)
+    sel = torch.topk(probs, K).indices.tolist()
+    gate, up, down = _host_experts(weight_buf, E, H, I, sel, dtype)
+    for _ in range(max(0, warmup)):
         tc.moe_forward(xh, gwh, gate, up, down, K, bh)
     times = []
     t_end = time.perf_counter() + budget_s
@@ -212,15 +235,53 @@ def cpu_composition_timing(x, gate_w, weight_buf, E, H, I, K, budget_s, max_call
         t0 = time.perf_counter()
         tc.moe_forward(xh, gwh, gate, up, down, K, bh)
         times.append(time.perf_counter() - t0)
+    if not times:  # the budget ran out in the warm-up: one timed call
+        t0 = time.perf_counter()
+        tc.moe_forward(xh, gwh, gate, up, down, K, bh)
+        times.append(time.perf_counter() - t0)
     return statistics.median(times) * 1e6, len(times), threads
 
 
+def cpu_reference_output(x, gate_w, weight_buf, E, H, I, K, bias=None):
+    """The restated torch composition's fp32 output and selected experts for
+    one token (the parity checker of the bench line)."""
+    tc = _composition()
+    torch.set_num_threads(os.cpu_count() or 1)
+    xh = x.detach().float().cpu()
+    gwh = gate_w.detach().float().cpu()
+    bh = None if bias is None else bias.detach().float().cpu()
+    probs = torch.softmax(gwh @ xh + (bh if bh is not None else 0), dim=0)
+    sel = torch.topk(probs, K).indices.tolist()
+    gate, up, down = _host_experts(weight_buf, E, H, I, sel, torch.float32)
+    return tc.moe_forward(xh, gwh, gate, up, down, K, bh), sel
+
+
+def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.detach().double().cpu().reshape(-1), b.detach().double().cpu().reshape(-1)
+    den = torch.linalg.vector_norm(b).item()
+    return torch.linalg.vector_norm(a - b).item() / (den if den > 0 else 1.0)
+
+
 # ---------------------------------------------------------------------------
-def workload_name(args, world: int) -> str:
-    return f"{args.config}_bs1_{args.dtype}" + (f"_{args.parallel}{world}" if world > 1 else "")
+def workload_name(cfg: str, dtype: str, parallel: str, world: int) -> str:
+    return f"{cfg}_bs1_{dtype}" + (f"_{parallel}{world}" if world > 1 else "")
+
+
+def config_dict(cfg: str, dtype: str, parallel: str, world: int, allreduce: str) -> dict:
+    """The workload, identical in both arms' lines."""
+    E, H, I, K = SHAPES[cfg]
+    return {"workload": workload_name(cfg, dtype, parallel, world), "E": E, "H": H, "I": I,
+            "top_k": K, "tokens": 1, "dtype": dtype,
+            "parallelism": f"{parallel}{world}" if world > 1 else "single",
+            "allreduce": ((("fused in the layer kernel (NVLink peer memory)"
+                            if allreduce == "fused" else "NCCL") if world > 1 else None)),
+            "l2": "inputs larger than L2 (rotating layers, > 4x L2 streamed between reuses)"}
 
 
 def run_reference_arm(args, world, rank):
+    """warp-route's CPU composition (restated) on all host threads, on the
+    same workload as our arm: `--warmup` untimed forwards, then up to
+    `--steps` timed forwards within a bounded budget; rank 0 only."""
     if rank != 0:
         return
     from warp_route import synthetic
@@ -228,22 +289,19 @@ def run_reference_arm(args, world, rank):
     E, H, I, K = SHAPES[args.config]
     dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    L = synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=0)
-    budget = min(60.0, max(5.0, args.cpu_seconds))
+    L = synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100, layer=0)
+    budget = min(120.0, max(5.0, args.cpu_seconds))
     us, n, cores = cpu_composition_timing(L.x, L.gate_w, L.weight_buf, E, H, I, K, budget,
-                                          max_calls=args.steps)
-    sample = (f"{n} forwards of the {args.config} layer (bs=1, fp32 weights of the selected "
-              f"experts), median; warp-route's torch composition restated")
+                                          max_calls=args.steps, warmup=args.warmup)
+    sample = (f"{n} single-token forwards of the {args.config} layer (the selected experts "
+              f"widened to fp32, warp-route's only dtype), median after {args.warmup} warm-ups; "
+              f"warp-route's torch composition restated in oracle/torch_composition.py")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": "us/layer",
-        "n_gpus": args.gpus, "steps": n, "warmup": 3, "ms_per_step": round(us / 1000, 4),
-        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_name(args, world), "E": E, "H": H, "I": I, "top_k": K,
-                   "tokens": 1,
-                   "parallelism": f"{args.parallel}{world}" if world > 1 else "single",
-                   "reference_compute": "fp32 (warp-route's only dtype): the layer's "
-                                        f"{args.dtype} weights widened to fp32"},
+        "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
+        "ms_per_step": round(us / 1000, 5), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args.config, args.dtype, args.parallel, world, args.allreduce),
         "cpu_baseline": {"value": round(us, 2), "unit": "us/layer", "cores": cores,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(us, 2), "unit": "us/layer", "h2d_bytes_per_step": 0,
@@ -277,6 +335,7 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
               for li in range(nl)]
     results = []
     stream = torch.cuda.Stream()
+    rv_buf = torch.zeros(1, device=dev)
     for T in tokens:
         gx = torch.Generator(device=dev)
         gx.manual_seed(7000 + T)
@@ -318,10 +377,9 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
         for _ in range(2):
             g.replay()
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(dev.index) as clk:
+            start_together(world, stream, lambda: dist.all_reduce(rv_buf))
             t0.record(stream)
             with torch.cuda.stream(stream):
                 for _ in range(args.sweep_steps):
@@ -367,66 +425,110 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
             "results": results}
 
 
-def run_ours(args, world, rank, local):
+# The GPU stays busy this long (≈ 2 ms at up to 2 GHz) while the host
+# enqueues a timed region, so the region starts on the device, not when the
+# host gets there.
+SLEEP_CYCLES = 4_000_000
+
+
+def start_together(world, stream, collective):
+    """Device-side rendezvous in front of a timed region (N > 1).
+
+    The ranks leave the host barrier at different times (process scheduling,
+    the clock sampler's start-up), so an event recorded straight after it would
+    charge that skew to the region through the first collective.  Instead each
+    rank queues a sleep kernel (so the host has queued the whole region before
+    the device reaches it) and one untimed collective step; that step ends on
+    every rank when the slowest rank has joined, and the region's start event
+    is recorded right behind it."""
+    if world == 1:
+        return
+    import torch.distributed as dist
+
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(SLEEP_CYCLES)
+        collective()
+
+
+def measure_config(args, cfg, parallel, world, rank, local, dev, *, cpu_leg):
+    """Times one workload: one decode token through `cfg`'s layer per step
+    (tensor- or expert-parallel over the ranks), device-resident (`value`) and
+    end to end through the public API (`e2e`), and checks a sampled layer
+    against the CPU composition (and, N > 1, against the whole layer run on
+    rank 0's GPU).  Returns the dict that becomes the JSON line (rank 0)."""
     import torch.distributed as dist
 
     from warp_route import functional as F
     from warp_route import synthetic
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    E, H, I, K = SHAPES[args.config]
+    E, H, I, K = SHAPES[cfg]
     dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
     elt = 2 if dt == torch.bfloat16 else 4
-    tp = world if args.parallel == "tp" and world > 1 else 1
-    ep = world if args.parallel == "ep" and world > 1 else 1
+    tp = world if parallel == "tp" and world > 1 else 1
+    ep = world if parallel == "ep" and world > 1 else 1
+    if I % tp or E % ep:
+        raise SystemExit(f"{cfg}: cannot split I={I} over {tp} or E={E} over {ep} ranks")
+    Il = I // tp
     # Rotate enough layers that the bytes streamed between two reads of the
     # same layer exceed 4x L2 (cold HBM every step).
-    sel_bytes = K * 3 * H * (I // tp) * elt
+    sel_bytes = K * 3 * H * Il * elt
     n_layers = max(2, math.ceil(4 * L2_BYTES / max(1, sel_bytes)) + 1)
-    layer_bytes = E // ep * 3 * H * (I // tp) * elt
+    layer_bytes = E // ep * 3 * H * Il * elt
     n_layers = min(n_layers, max(2, int(100e9 // layer_bytes)))
     if args.layers > 0:
         n_layers = args.layers
-    layers = []
-    for li in range(n_layers):
-        layers.append(synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100 + li,
-                                           layer=li, tp_rank=rank if tp > 1 else 0, tp_size=tp,
-                                           ep_rank=rank if ep > 1 else 0, ep_size=ep))
-    Il = I // tp
+    layers = [synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100 + li, layer=li,
+                                   tp_rank=rank if tp > 1 else 0, tp_size=tp,
+                                   ep_rank=rank if ep > 1 else 0, ep_size=ep)
+              for li in range(n_layers)]
 
-    # routing of each layer (identical on all ranks) -> algorithmic bytes
-    distinct = []
+    # Routing of each layer (identical on all ranks) -> algorithmic bytes of
+    # the busiest rank (expert parallel: the rank holding the most selected
+    # experts sets the layer's time) and of all ranks together.
+    busiest, total = [], []
     for Lr in layers:
         _, ids, _ = F.fused_moe_routed(Lr.x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
                                        ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)
         sel = set(ids.cpu().view(-1).tolist())
-        if ep > 1:
-            sel = {e for e in sel if Lr.ep_first <= e < Lr.ep_first + Lr.ep_num}
-        distinct.append(len(sel))
-    bytes_per_layer = [synthetic.algorithmic_bytes(E, H, Il, u, 1, elt) for u in distinct]
-    avg_bytes = sum(bytes_per_layer) / len(bytes_per_layer)
+        per_rank = [len([e for e in sel if r * (E // ep) <= e < (r + 1) * (E // ep)])
+                    for r in range(ep)]
+        busiest.append(synthetic.algorithmic_bytes(E, H, Il, max(per_rank), 1, elt))
+        total.append(sum(synthetic.algorithmic_bytes(E, H, Il, u, 1, elt) for u in per_rank)
+                     if ep > 1 else world * busiest[-1])
+    avg_bytes = sum(busiest) / len(busiest)
+    avg_total = sum(total) / len(total)
 
     # N > 1: every rank's partial output is summed inside the layer kernel
     # (PeerComm, NVLink peer memory), or by a separate NCCL all-reduce.
     fused_ar = world > 1 and args.allreduce == "fused"
     comm = F.PeerComm(H) if fused_ar else None
 
-    def layer(Lr, x):
+    def layer(Lr, x, routing=False):
         if fused_ar:
-            return F.fused_moe_allreduce(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K, comm,
-                                         ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)
-        if ep > 1:
-            return F.fused_moe_routed(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
-                                      ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num)[0]
+            r = F.fused_moe_allreduce(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K, comm,
+                                      ep_first_expert=Lr.ep_first, ep_num_local=Lr.ep_num,
+                                      return_routing=True)
+            return (r[0], r[1]) if routing else r[0]
+        if ep > 1 or routing:
+            out, ids, _ = F.fused_moe_routed(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K,
+                                             ep_first_expert=Lr.ep_first,
+                                             ep_num_local=Lr.ep_num)
+            return (out, ids) if routing else out
         return F.fused_moe(x, Lr.gate_w, Lr.weight_buf, E, H, Il, K)
 
     def reduce(out):
         if world > 1 and not fused_ar:
             dist.all_reduce(out)
+
+    rv_buf = torch.zeros(1, device=dev)
+
+    def rendezvous_step():
+        if fused_ar:
+            layer(layers[0], layers[0].x)
+        else:
+            dist.all_reduce(rv_buf)
 
     stream = torch.cuda.current_stream()
     W, Ksteps = args.warmup, args.steps
@@ -441,14 +543,13 @@ def run_ours(args, world, rank, local):
     # duration is the timed region over the launches (launch gaps included);
     # per-step events would sit between the kernels and stretch them.  With
     # a separate NCCL all-reduce, each layer call is bracketed by its own
-    # events.
+    # events.  Serving replays decode steps from CUDA graphs: the timed steps
+    # are replays of a graph of the rotating layers' calls (exactly K calls;
+    # capture and warm-up happen before the timed region); the NCCL
+    # comparison runs eagerly.
     per_step = world > 1 and not fused_ar
-    # Serving replays decode steps from CUDA graphs: the timed steps are
-    # replays of a graph of the rotating layers' calls (exactly K calls;
-    # capture and warm-up happen before the timed region).  The NCCL
-    # all-reduce comparison runs eagerly.
     use_graph = not args.no_graph and not per_step
-    graphs = []
+    graphs, cap_stream = [], None
     if use_graph:
         cap_stream = torch.cuda.Stream()
         with torch.cuda.stream(cap_stream):  # warm up on the capture stream (its workspace)
@@ -474,10 +575,8 @@ def run_ours(args, world, rank, local):
     k_start = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     k_end = [torch.cuda.Event(enable_timing=True) for _ in range(Ksteps if per_step else 0)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        start_together(world, stream, rendezvous_step)
         t0.record(stream)
         if use_graph:
             for g in graphs:
@@ -493,8 +592,6 @@ def run_ours(args, world, rank, local):
                 reduce(out)
         t1.record(stream)
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     clocks = clk.summary()
     total_ms = t0.elapsed_time(t1)
     if per_step:
@@ -502,11 +599,6 @@ def run_ours(args, world, rank, local):
         kern_avg_ms = sum(kern_ms) / len(kern_ms)
     else:
         kern_avg_ms = total_ms / Ksteps
-    t = torch.tensor([total_ms, kern_avg_ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, kern_avg_ms = t.tolist()
-    us_per_layer = total_ms * 1000.0 / Ksteps
 
     # ---- end-to-end through the public API, host buffers in and out ----
     # Every step copies its token in from pinned host memory and its output
@@ -544,11 +636,11 @@ def run_ours(args, world, rank, local):
     for i in range(min(W, 8)):
         e2e_step(i)
     torch.cuda.synchronize()
-    # Serving replays its steps from CUDA graphs: unless --no-graph, the timed
-    # e2e steps are replays of a graph of E2E_CHUNK steps, each step the same
-    # three operations (pinned-host -> device copy of its token, the public
-    # layer call, device -> pinned-host copy of its output) on the same three
-    # streams, ordered by the same events (graph edges after capture).
+    # Unless --no-graph, the timed e2e steps are replays of a graph of
+    # E2E_CHUNK steps, each step the same three operations (pinned-host ->
+    # device copy of its token, the public layer call, device -> pinned-host
+    # copy of its output) on the same three streams, ordered by the same
+    # events (graph edges after capture).
     e2e_graphs = []
     if use_graph:
         cap2 = torch.cuda.Stream()
@@ -586,9 +678,8 @@ def run_ours(args, world, rank, local):
         e2e_graphs = [g_e2e] * (Ke // chunk) + ([capture_e2e(rem)] if rem else [])
         g_e2e.replay()
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start_together(world, stream, rendezvous_step)
     e0.record(stream)
     if use_graph:
         for g in e2e_graphs:
@@ -600,81 +691,181 @@ def run_ours(args, world, rank, local):
         stream.wait_stream(d2h)
     e1.record(stream)
     torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    e2e_ms = e0.elapsed_time(e1)
+
+    # per-rank times -> max over ranks (the job's time) and the spread
+    mine = torch.tensor([total_ms, kern_avg_ms, e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_us = te.item() * 1000.0 / Ke
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        every = torch.stack(every).cpu()
+    else:
+        every = mine.cpu().unsqueeze(0)
+    total_ms, kern_avg_ms, e2e_ms = every.max(dim=0).values.tolist()
+    spread_us = ((every[:, 0].max() - every[:, 0].min()).item() * 1000.0 / Ksteps)
+
     # A bounded device wait that gave up would make the timings meaningless.
-    status = F._load_extension().workspace_status(layers[0].x)
+    ext = F._load_extension()
+    status = ext.workspace_status(layers[0].x)
     if use_graph:
         with torch.cuda.stream(cap_stream):  # the workspace the graph's launches used
-            status = status or F._load_extension().workspace_status(layers[0].x)
-    if status != 0:
-        raise SystemExit(f"fused kernel reported device status {status}: timing discarded")
-
-    # ---- CPU baseline (rank 0, N = 1 only) ----
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        full = layers[0]
-        us_cpu, ncalls, cores = cpu_composition_timing(full.x, full.gate_w, full.weight_buf, E, H,
-                                                       Il, K, args.cpu_seconds)
-        cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
-               "sample": f"{ncalls} single-token forwards of layer 0 ({args.config}), the "
-                         f"selected experts widened to fp32, median of {ncalls} after 3 warm-ups; "
-                         f"warp-route's torch composition restated in oracle/torch_composition.py"}
-
-    # The sweep sums the ranks' batch outputs with NCCL: measured faster than the
-    # all-reducing combine step for batches (2 GPUs, 8 layers: 250 vs 260 µs
-    # at T = 16, 428 vs 456 µs at T = 256); `--sweep-fused-allreduce` uses the
-    # combine step instead.
-    sweep = batched_sweep(args, dev, world, rank,
-                          comm if args.sweep_fused_allreduce else None)
-
+            status = status or ext.workspace_status(layers[0].x)
+    st = torch.tensor([status], device=dev)
     if world > 1:
-        dist.barrier()
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+    if st.item() != 0:
+        raise SystemExit(f"{cfg}: a fused kernel reported device status {st.item()}: "
+                         "timing discarded")
+
+    # ---- parity of a sampled layer (layer 0), through the timed path ----
+    L0 = layers[0]
+    out0, ids0 = layer(L0, L0.x, routing=True)
+    reduce(out0)
+    torch.cuda.synchronize()
+    parity = {"sampled_layer": 0, "tolerance_rel_l2": 1e-3}
+    ok = True
+    if world > 1:
+        every_out = [torch.empty_like(out0) for _ in range(world)]
+        dist.all_gather(every_out, out0)
+        parity["ranks_identical"] = all(torch.equal(every_out[0], o) for o in every_out[1:])
+        ok = ok and parity["ranks_identical"]
+    full = None
     if rank == 0:
-        peak, peak_kind = peaks()
-        # the fused kernel's bytes per launch on the busiest rank (identical per rank for TP)
-        achieved = avg_bytes / (kern_avg_ms * 1e-3) / 1e9
-        workload = workload_name(args, world)
-        traffic = ncu_traffic(workload)
-        line = {
-            "metric": METRIC, "value": round(us_per_layer, 3), "unit": "us/layer",
-            "n_gpus": world, "steps": Ksteps, "warmup": W,
-            "ms_per_step": round(total_ms / Ksteps, 6), "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
-            "config": {"workload": workload, "E": E, "H": H, "I": I, "top_k": K, "tokens": 1,
-                       "parallelism": f"{args.parallel}{world}" if world > 1 else "single",
-                       "allreduce": (("fused in the layer kernel (NVLink peer memory)"
-                                      if fused_ar else "NCCL") if world > 1 else None),
-                       "l2": f"inputs larger than L2: {n_layers} rotating layers, "
-                             f"{avg_bytes / 1e6:.1f} MB streamed per step",
-                       "layers_rotated": n_layers,
-                       "timing": ("CUDA-graph replay of the layer calls" if use_graph
-                                  else "eager layer calls")},
-            "hbm_gbs": round(avg_bytes / (us_per_layer * 1e-6) / 1e9, 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind,
-                         "traffic": traffic,
-                         "kernel_us": round(kern_avg_ms * 1000, 3),
-                         "algorithmic_bytes": int(avg_bytes)},
-            "e2e": {"value": round(e2e_us, 3), "unit": "us/layer",
-                    "h2d_bytes_per_step": H * elt * world,
-                    "d2h_bytes_per_step": H * 4 * world,
-                    "timing": ("CUDA-graph replays of [H2D copy, layer call, D2H copy] steps"
-                               if use_graph else "eager steps")},
-            "gpu_launches": Ksteps,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-        }
-        if sweep is not None:
-            line["batched_sweep"] = sweep
-        print(json.dumps(line), flush=True)
+        if world > 1:
+            full = synthetic.make_layer(E, H, I, K, dtype=dt, device=dev, seed=100, layer=0)
+            r_out, r_ids, _ = F.fused_moe_routed(full.x, full.gate_w, full.weight_buf, E, H, I, K)
+            torch.cuda.synchronize()
+            m = {"ids_match": r_ids.view(-1).tolist() == ids0.view(-1).tolist(),
+                 "rel_l2": float(f"{rel_l2(out0, r_out):.3e}")}
+            parity["vs_whole_layer_on_rank0_gpu"] = m
+            ok = ok and m["ids_match"] and m["rel_l2"] <= 1e-3
+        src = full if full is not None else L0
+        c_out, c_sel = cpu_reference_output(src.x, src.gate_w, src.weight_buf, E, H, I, K)
+        m = {"ids_match": c_sel == ids0.view(-1).tolist(),
+             "rel_l2": float(f"{rel_l2(out0, c_out):.3e}")}
+        parity["vs_cpu_composition"] = m
+        ok = ok and m["ids_match"] and m["rel_l2"] <= 1e-3
+        parity["ok"] = bool(ok)
+    del full
+
+    # ---- CPU baseline (rank 0, N = 1, the line's own workload) ----
+    cpu = None
+    if cpu_leg and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        us_cpu, ncalls, cores = cpu_composition_timing(L0.x, L0.gate_w, L0.weight_buf, E, H, Il,
+                                                       K, args.cpu_seconds)
+        variants = []
+        for thr, cdt, name in ((1, torch.float32, "fp32"), (None, torch.bfloat16, "bf16")):
+            v_us, v_n, v_thr = cpu_composition_timing(L0.x, L0.gate_w, L0.weight_buf, E, H, Il,
+                                                      K, min(6.0, args.cpu_seconds),
+                                                      threads=thr, dtype=cdt)
+            variants.append({"value": round(v_us, 1), "unit": "us/layer", "cores": v_thr,
+                             "dtype": name, "calls": v_n})
+        cpu = {"value": round(us_cpu, 1), "unit": "us/layer", "cores": cores, "kind": "port",
+               "dtype": "fp32",
+               "sample": f"{ncalls} single-token forwards of layer 0 ({cfg}), the selected experts "
+                         f"widened to fp32, median after 3 warm-ups; warp-route's torch "
+                         f"composition restated in oracle/torch_composition.py",
+               "variants": variants}
+
     if comm is not None:
         torch.cuda.synchronize()
         dist.barrier()
         comm.close()
+    graphs.clear()
+    e2e_graphs.clear()
+    del layers
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+    us_per_layer = total_ms * 1000.0 / Ksteps
+    peak, peak_kind = peaks()
+    achieved = avg_bytes / (kern_avg_ms * 1e-3) / 1e9
+    workload = workload_name(cfg, args.dtype, parallel, world)
+    res = {
+        "value": round(us_per_layer, 3), "unit": "us/layer",
+        "ms_per_step": round(total_ms / Ksteps, 6),
+        "config": config_dict(cfg, args.dtype, parallel, world, args.allreduce),
+        "method": {"layers_rotated": n_layers,
+                   "mb_streamed_per_step_busiest_rank": round(avg_bytes / 1e6, 1),
+                   "timing": ("CUDA-graph replay of the layer calls" if use_graph
+                              else "eager layer calls") +
+                             ("; device-side rendezvous (sleep + one untimed collective layer "
+                              "call) before each timed region" if world > 1 else ""),
+                   "rank_spread_us_per_layer": round(spread_us, 3) if world > 1 else 0.0},
+        "hbm_gbs": round(avg_bytes / (us_per_layer * 1e-6) / 1e9, 1),
+        "hbm_gbs_all_ranks": round(avg_total / (us_per_layer * 1e-6) / 1e9, 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": ncu_traffic(workload),
+                     "kernel_us": round(kern_avg_ms * 1000, 3),
+                     "algorithmic_bytes": int(avg_bytes),
+                     "bytes_note": "selected local experts' weights + router + x + fp32 out, "
+                                   "of the rank with the most selected experts"},
+        "e2e": {"value": round(e2e_ms * 1000.0 / Ke, 3), "unit": "us/layer",
+                "h2d_bytes_per_step": H * elt * world,
+                "d2h_bytes_per_step": H * 4 * world,
+                "timing": ("CUDA-graph replays of [H2D copy, layer call, D2H copy] steps"
+                           if use_graph else "eager steps")},
+        "parity": parity,
+        "gpu_launches": Ksteps,
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        res["cpu_baseline"] = cpu
+    return res
+
+
+def run_ours(args, world, rank, local):
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    main = measure_config(args, args.config, args.parallel, world, rank, local, dev, cpu_leg=True)
+    extras = {}
+    for cfg in [c for c in args.extra_configs.split(",") if c.strip()]:
+        if cfg == args.config:
+            continue
+        # the other BASELINE configurations: expert parallel over N > 1 GPUs
+        r = measure_config(args, cfg, "ep", world, rank, local, dev, cpu_leg=False)
+        extras[r["config"]["workload"]] = r
+
+    sweep = None
+    if args.sweep_tokens.strip():
+        # The sweep sums the ranks' batch outputs with NCCL: measured faster
+        # than the all-reducing combine step for batches (2 GPUs, 8 layers:
+        # 250 vs 260 µs at T = 16, 428 vs 456 µs at T = 256);
+        # `--sweep-fused-allreduce` uses the combine step instead.
+        from warp_route import functional as F
+        comm = F.PeerComm(SHAPES["mixtral"][1]) if (args.sweep_fused_allreduce and world > 1) \
+            else None
+        sweep = batched_sweep(args, dev, world, rank, comm)
+        if comm is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            comm.close()
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC}
+        line.update({k: main[k] for k in ("value", "unit")})
+        line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                     "ms_per_step": main["ms_per_step"], "higher_is_better": False,
+                     "scaling": "strong", "vs_baseline": None, "dtype": args.dtype,
+                     "data": "synthetic"})
+        for k in ("config", "method", "hbm_gbs", "hbm_gbs_all_ranks", "roofline", "e2e",
+                  "parity", "gpu_launches", "clocks"):
+            line[k] = main[k]
+        line["cpu_baseline"] = main.get("cpu_baseline")
+        if extras:
+            line["other_configs"] = extras
+        if sweep is not None:
+            line["batched_sweep"] = sweep
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

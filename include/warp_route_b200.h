@@ -148,15 +148,22 @@ WR_API wr_status_t wr_fused_moe(const wr_moe_desc_t* desc, const void* x,
  * library holds until the process exits; a layer that needs more (about
  * top_k * intermediate_dim * 4 + 8704 bytes) gets WR_ERR_UNSUPPORTED and
  * nothing is launched.  All calls on one device share the array and its
- * control words are cleared on `stream` before each launch, so calls that
+ * counters are cleared on `stream` before each launch, so calls that
  * overlap on the GPU race: serialise them.  The first call on each device
  * looks up the array's device address; make that call before any stream
- * capture.  No counterpart in warp-route. */
+ * capture.  A bounded wait that gives up inside a call sets the array's
+ * status word, which the calls themselves never clear: read it with
+ * wr_fused_moe_noalloc_status.  No counterpart in warp-route. */
 WR_API wr_status_t wr_fused_moe_noalloc(const wr_moe_desc_t* desc, const void* x,
                                         const void* gate_w, const void* weight_buf,
                                         int64_t weight_buf_bytes, float* out,
                                         int32_t* topk_ids, float* topk_weights,
                                         wr_stream_t stream);
+/* Reads (and clears) the status word of the built-in scratch that
+ * wr_fused_moe_noalloc uses on the current device: WR_OK, or WR_ERR_TIMEOUT
+ * when a bounded wait inside one of the calls since the last read gave up.
+ * Synchronises `stream`; allocates nothing.  No counterpart in warp-route. */
+WR_API wr_status_t wr_fused_moe_noalloc_status(wr_stream_t stream);
 
 /* ---- fused layer, a batch of tokens ----------------------------------- */
 
@@ -183,8 +190,13 @@ WR_API wr_status_t wr_batched_fused_moe(const wr_moe_desc_t* desc, int32_t num_t
  *   among the ranks (any host-side channel) -> wr_comm_open with all of them
  *   in rank order.
  * Every rank must then make the same sequence of wr_fused_moe_allreduce
- * calls; a rank that stops makes the others' bounded waits give up
- * (WR_ERR_TIMEOUT through wr_workspace_status) instead of hanging. */
+ * calls.  A rank that stops makes the others' bounded waits for its partial
+ * outputs give up after the peer timeout (2 s unless set with
+ * wr_comm_set_peer_timeout_ns) instead of hanging: the call's output is then
+ * wrong and wr_workspace_status reports WR_ERR_TIMEOUT.  After that the
+ * ranks' launch counters differ and every later call would time out too:
+ * recover with wr_comm_reset on every rank, between two host barriers, with
+ * no layer call in flight (or destroy and recreate the communicators). */
 typedef struct wr_comm* wr_comm_t;
 
 /* Bytes of one rank's handle (a CUDA IPC memory handle). */
@@ -195,6 +207,18 @@ WR_API wr_status_t wr_comm_get_handle(wr_comm_t comm, void* handle);
 /* handles: world_size * wr_comm_handle_bytes() bytes, rank order. */
 WR_API wr_status_t wr_comm_open(wr_comm_t comm, const void* handles);
 WR_API wr_status_t wr_comm_destroy(wr_comm_t comm);
+/* Bound of each wait for a peer rank's partial outputs, in ns (0: the
+ * default, 2 s).  Takes effect from the next call; a CUDA graph keeps the
+ * bound its launches were captured with. */
+WR_API wr_status_t wr_comm_set_peer_timeout_ns(wr_comm_t comm, uint64_t ns);
+/* Puts this rank's launch counter and mailbox back to their initial state
+ * (zero), on `stream`, and synchronises it.  After a call that timed out on
+ * any rank: every rank waits at a host barrier until no layer call of any
+ * rank is in flight, calls wr_comm_reset, and waits at a second host barrier
+ * before its next wr_fused_moe_allreduce (no rank may store into a mailbox
+ * that its owner has not reset yet).  The current device must be the
+ * communicator's. */
+WR_API wr_status_t wr_comm_reset(wr_comm_t comm, wr_stream_t stream);
 
 /* num_tokens tokens through this rank's shard of the layer (a tensor-
  * parallel slice of every expert's intermediate dimension, or an

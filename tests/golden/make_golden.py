@@ -9,7 +9,14 @@ checkout, on the reference's own test configurations:
                                     calls, so the golden is the composition
                                     applied per token),
   - the benchmark's tiny CPU configuration (H512 I1024 E8 k2, seed 0),
-plus bf16-rounded variants (inputs rounded to bf16, composition run in fp32).
+plus bf16-rounded variants (inputs rounded to bf16, composition run in fp32),
+and cases the reference's CUDA kernels cannot run but its composition can:
+  - top_k 4, 6 and 8 (the fused kernels stop at 2, src/bindings.cpp:75,117),
+    on the single-token test inputs with E up to 64;
+  - bf16-rounded token batches (the grouped tensor-core path of this build):
+    E8 k2 B16, E16 k4 B64, E64 k6 B5;
+  - the DeepSeek-shaped benchmark layer (H2048 I1408 E64 k6, the benchmark
+    init with seed 0, bf16-rounded).
 
 Indices and weights are taken with the same torch ops the composition uses
 (gate_w @ x, softmax, torch.topk).  The reference checkout is needed only
@@ -37,6 +44,10 @@ BATCHED = [(8, 256, 512, 1, b) for b in (1, 4, 16, 64)] + \
           [(8, 256, 512, 2, b) for b in (1, 4, 16, 64)] + \
           [(16, 512, 1024, 2, b) for b in (1, 4, 16)]
 BF16_SINGLE = [(8, 512, 1024, 2), (16, 256, 512, 2), (8, 1024, 2048, 2)]
+TOPK_SINGLE = [(8, 256, 512, 4), (16, 256, 512, 6), (16, 512, 1024, 8), (64, 256, 512, 6),
+               (64, 512, 1024, 8)]
+BF16_BATCHED = [(8, 512, 1024, 2, 16), (16, 512, 1024, 4, 64), (64, 256, 512, 6, 5)]
+DEEPSEEK = (64, 2048, 1408, 6)
 
 
 def load_reference(ref_root: str):
@@ -101,6 +112,28 @@ def main():
         emit(f"bf16_E{E}_H{H}_I{I}_k{k}",
              dict(kind="single", gen="reference_test_inputs", E=E, H=H, I=I, seed=42,
                   tokens=1, bf16=True), x, gw, ex, k)
+
+    for (E, H, I, k) in TOPK_SINGLE:
+        x, gw, ex = gi.reference_test_inputs(E, H, I, 42)
+        emit(f"topk_E{E}_H{H}_I{I}_k{k}",
+             dict(kind="single", gen="reference_test_inputs", E=E, H=H, I=I, seed=42,
+                  tokens=1, bf16=False), x, gw, ex, k)
+    rb = gi.round_bf16
+    for (E, H, I, k, B) in BF16_BATCHED:
+        x, gw, ex = gi.reference_batched_inputs(E, H, I, B, 42)
+        x, gw = rb(x), rb(gw)
+        ex = tuple([rb(t) for t in lst] for lst in ex)
+        emit(f"bf16_batched_E{E}_H{H}_I{I}_k{k}_B{B}",
+             dict(kind="batched", gen="reference_batched_inputs", E=E, H=H, I=I, seed=42,
+                  tokens=B, bf16=True), x, gw, ex, k)
+    E, H, I, k = DEEPSEEK
+    x, gw, ex = gi.baseline_inputs(E, H, I, 0)
+    x, gw = rb(x), rb(gw)
+    ex = tuple([rb(t) for t in lst] for lst in ex)
+    emit(f"deepseek_bf16_E{E}_H{H}_I{I}_k{k}",
+         dict(kind="single", gen="baseline_inputs", E=E, H=H, I=I, seed=0, tokens=1,
+              bf16=True), x, gw, ex, k)
+    del ex
 
     arrays["index_json"] = np.frombuffer(json.dumps(index).encode(), dtype=np.uint8)
     np.savez_compressed(args.out, **arrays)

@@ -69,14 +69,53 @@ def test_pack_matches_oracle_layout(dtype):
     np.testing.assert_array_equal(raw, ref)
 
 
-def test_moelayer_pack_is_cached_until_a_parameter_changes():
-    layer = warp_route.MoELayer(2, 16, 32, top_k=1)
+def test_moelayer_parameters_are_the_packed_buffer():
+    """The expert parameters are views of the packed buffer: in-place writes
+    (including through .data, the usual checkpoint-loading idiom, and
+    load_state_dict) show up in it without a repack."""
+    E, H, I = 2, 16, 32
+    layer = warp_route.MoELayer(E, H, I, top_k=1)
     a = layer._pack_weights()
     assert layer._pack_weights() is a
+    n = H * I
+    stride = F._expert_stride_elems(H, I, 4)
     with torch.no_grad():
         layer.up_proj[1].add_(1.0)
+    assert layer._pack_weights() is a
+    assert torch.equal(a[stride + n:stride + 2 * n], layer.up_proj[1].detach().reshape(-1))
+    w = torch.randn(I, H)
+    layer.gate_proj[0].data.copy_(w)
+    assert layer._pack_weights() is a and torch.equal(a[:n].view(I, H), w)
+    sd = {k: v.clone() for k, v in layer.state_dict().items()}
+    sd["down_proj.1"] = torch.full((H, I), 3.0)
+    layer.load_state_dict(sd)
+    assert layer._pack_weights() is a
+    assert torch.equal(a[stride + 2 * n:stride + 3 * n], torch.full((H * I,), 3.0))
+    # the stride padding stays zero
+    assert stride == 3 * n  # 16 x 32 floats: already 128-byte aligned here
+
+
+def test_moelayer_repacks_when_parameters_move():
+    """A parameter that is no longer a view of the buffer (assigned a new
+    tensor, or converted by module.to) makes the next pack rebuild the buffer
+    from the parameters and re-point them at it."""
+    E, H, I = 2, 16, 41  # expert blocks not a multiple of 128 bytes: padded strides
+    layer = warp_route.MoELayer(E, H, I, top_k=2)
+    a = layer._pack_weights()
+    w = torch.randn(H, I)
+    layer.down_proj[0].data = w.clone()
     b = layer._pack_weights()
     assert b is not a
-    n = 16 * 32
-    stride = F._expert_stride_elems(16, 32, 4)
-    assert torch.equal(b[stride + n:stride + 2 * n], layer.up_proj[1].detach().reshape(-1))
+    stride = F._expert_stride_elems(H, I, 4)
+    n = H * I
+    assert torch.equal(b[2 * n:3 * n].view(H, I), w)
+    assert layer.down_proj[0].data_ptr() == b[2 * n:].data_ptr()
+    assert layer._pack_weights() is b
+    layer.to(torch.bfloat16)
+    c = layer._pack_weights()
+    assert c.dtype == torch.bfloat16 and c is not b
+    assert torch.equal(c[2 * n:3 * n].view(H, I), w.to(torch.bfloat16))
+    assert all(p.dtype == torch.bfloat16 for p in layer.parameters())
+    # bf16 stride rounding: the padding between experts is zero
+    sb = F._expert_stride_elems(H, I, 2)
+    assert sb > 3 * n and torch.count_nonzero(c[3 * n:sb]) == 0

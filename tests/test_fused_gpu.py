@@ -16,7 +16,7 @@ import torch
 
 import inputs as gi
 import oracle
-from conftest import golden_inputs, load_golden
+from conftest import golden_inputs, golden_selected, load_golden
 from warp_route import _abi, synthetic
 from wr_testlib import abi_layer, host_array, oracle_inputs_from_device, ptr, stream_ptr
 
@@ -55,14 +55,22 @@ def test_golden_cases_through_c_abi(golden, meta):
     E, H, I, K = meta["E"], meta["H"], meta["I"], meta["top_k"]
     xd = x.to(dt).cuda()
     gwd = gw.to(dt).cuda().contiguous()
-    wb = torch.from_numpy(gi.pack_numpy(ex, bf16=meta["bf16"])).cuda().view(dt)
+    # the experts the reference selected are packed (the others stay zero: a
+    # wrong selection reads zeros and fails the output check as well)
+    wb = torch.from_numpy(gi.pack_numpy(ex, bf16=meta["bf16"],
+                                        only=golden_selected(z, meta))).cuda().view(dt)
     xin = xd if meta["kind"] == "batched" else xd[0].contiguous()
     out, ids, w = abi_layer(xin, gwd, wb, E, H, I, K)
     torch.cuda.synchronize()
-    _check(out, ids, w, xin, gwd, wb, E, H, I, K, golden_ids=z[meta["name"] + "/ids"])
-    # and directly against the reference composition's own output
+    # directly against the reference composition's own selection and output
+    golden_ids = z[meta["name"] + "/ids"]
+    np.testing.assert_array_equal(ids.cpu().numpy().reshape(golden_ids.shape), golden_ids)
+    np.testing.assert_allclose(w.cpu().numpy().reshape(golden_ids.shape),
+                               z[meta["name"] + "/weights"], rtol=1e-5, atol=1e-7)
     ref = z[meta["name"] + "/out"]
     assert oracle.rel_l2(out.cpu().numpy().reshape(ref.shape), ref) <= REL_L2_TOL
+    # and against the oracle
+    _check(out, ids, w, xin, gwd, wb, E, H, I, K, golden_ids=golden_ids)
 
 
 @pytest.mark.parametrize("shape,dtype", [("tiny", torch.float32), ("mixtral", torch.bfloat16),
@@ -216,3 +224,44 @@ def test_empty_batch_is_a_no_op():
     st = lib.wr_batched_fused_moe(ctypes.byref(d), 0, ptr(L.x), ptr(L.gate_w), ptr(L.weight_buf),
                                   L.weight_buf.numel() * 4, None, None, None, None, 0, stream_ptr())
     assert st == _abi.WR_OK
+
+
+@pytest.mark.parametrize("mode", ["tp", "ep"])
+def test_one_rank_allreduce_tail_matches_plain_layer(mode):
+    """The all-reduce fused into the streaming kernel's tail, given a one-rank
+    communicator: every CTA stores its rows as tagged words into the mailbox
+    and polls them back, so the output must equal the plain single-token
+    layer's (the sum of one source adds 0).  Shards as the 8-GPU runs hold
+    them: a tensor-parallel slice of the Mixtral shape (I / 8) and an
+    expert-parallel set of the DeepSeek shape (8 of 64 experts).  Three calls
+    in a row cover both mailbox parities and the epoch advancing."""
+    from warp_route import functional as F
+    if mode == "tp":
+        E, H, I, K = synthetic.SHAPES["mixtral"]
+        sh = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=83, tp_rank=3,
+                                  tp_size=8)
+    else:
+        E, H, I, K = synthetic.SHAPES["deepseek"]
+        sh = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=83, ep_rank=2,
+                                  ep_size=8)
+    _C = F._load_extension()
+    comm = _C.comm_create(0, 1, H)
+    try:
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(5)
+        for _ in range(3):
+            x = torch.randn(H, generator=gen, device="cuda").to(torch.bfloat16)
+            ref, ref_ids, _ = F.fused_moe_routed(x, sh.gate_w, sh.weight_buf, E, H, sh.I, K,
+                                                 ep_first_expert=sh.ep_first,
+                                                 ep_num_local=sh.ep_num)
+            got, ids, _ = _C.fused_moe_allreduce(x, sh.gate_w, sh.weight_buf, E, H, sh.I, K,
+                                                 comm, None, sh.ep_first, sh.ep_num)
+            torch.cuda.synchronize()
+            assert torch.equal(ids, ref_ids)
+            assert torch.equal(got, ref), "one-rank all-reduce changed the output"
+        assert F._load_extension().workspace_status(x) == 0
+    finally:
+        _C.comm_destroy(comm)
+    # and the shard itself against the oracle
+    _check(got, None, None, x, sh.gate_w, sh.weight_buf, E, H, sh.I, K, ep_first=sh.ep_first,
+           ep_num=sh.ep_num)

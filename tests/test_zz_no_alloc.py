@@ -47,6 +47,8 @@ def _run_noalloc(lib, d, x, gate_w, wbuf, K):
     wbytes = wbuf.numel() * wbuf.element_size()
     _abi.check(lib.wr_fused_moe_noalloc(ctypes.byref(d), ptr(x), ptr(gate_w), ptr(wbuf), wbytes,
                                         ptr(out), ptr(ids), ptr(w), stream_ptr()))
+    # no bounded wait inside the call gave up
+    _abi.check(lib.wr_fused_moe_noalloc_status(stream_ptr()))
     return out, ids, w
 
 

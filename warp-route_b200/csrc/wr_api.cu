@@ -268,7 +268,7 @@ wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num_tokens
   if ((st = check_weights(p, weight_buf, weight_buf_bytes)) != WR_OK) return st;
   if ((st = check_ws(workspace, workspace_bytes, fused_ws_for(p))) != WR_OK) return st;
   return run_layer(p, x, gate_w, weight_buf, out, topk_ids, topk_weights, workspace,
-                   static_cast<cudaStream_t>(stream), v.world > 1 ? &v : nullptr);
+                   static_cast<cudaStream_t>(stream), &v);
 }
 
 size_t wr_naive_moe_workspace_size(const wr_moe_desc_t* desc) {

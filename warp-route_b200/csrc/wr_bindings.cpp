@@ -278,6 +278,16 @@ void comm_open(int64_t comm, torch::Tensor handles) {
 
 void comm_destroy(int64_t comm) { check_status(wr_comm_destroy(reinterpret_cast<wr_comm_t>(comm))); }
 
+void comm_set_peer_timeout_ns(int64_t comm, int64_t ns) {
+  TORCH_CHECK(ns >= 0, "peer timeout must be >= 0 ns");
+  check_status(wr_comm_set_peer_timeout_ns(reinterpret_cast<wr_comm_t>(comm), (uint64_t)ns));
+}
+
+void comm_reset(int64_t comm) {
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  check_status(wr_comm_reset(reinterpret_cast<wr_comm_t>(comm), stream));
+}
+
 // This rank's shard of the layer with the ranks' outputs summed in-kernel:
 // (out fp32 [..,H], ids int32 [T,K], weights fp32 [T,K]).
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_moe_allreduce(
@@ -379,6 +389,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_handle", &comm_handle, "This rank's IPC handle bytes (uint8 CPU tensor)");
   m.def("comm_open", &comm_open, "Map every rank's buffer (handles in rank order)");
   m.def("comm_destroy", &comm_destroy, "Unmap and free a communicator");
+  m.def("comm_set_peer_timeout_ns", &comm_set_peer_timeout_ns,
+        "Bound of each wait for a peer's partial outputs (ns; 0 = default)");
+  m.def("comm_reset", &comm_reset,
+        "Back to the initial state after a timed-out call (every rank, between host barriers)");
   m.def("fused_moe_allreduce", &fused_moe_allreduce,
         "This rank's shard of the layer with the ranks' outputs summed in the same kernel",
         py::arg("hidden"), py::arg("gate_w"), py::arg("weight_buf"), py::arg("num_experts"),

@@ -3,7 +3,7 @@
 //
 // Each rank allocates one device block at set-up — 256 bytes holding its
 // launch counter (epoch), then its mailbox of
-// [source rank][2 parities][4 tokens][H] 64-bit words — and shares it with
+// [source rank][2 parities][64 tokens][H] 64-bit words — and shares it with
 // the other ranks of the node through a CUDA IPC handle.  A fused launch
 // with epoch e on rank r stores each of its CTAs' partial output rows as
 // words (fp32 value | e << 32) into slot r of every rank's mailbox (peer
@@ -14,6 +14,13 @@
 // value: no flags or memory fences are needed.  Parity e & 1: a rank writes
 // a slot for launch e + 2 only after reading every rank's words of launch
 // e + 1, which each rank writes only after finishing launch e.
+//
+// A wait for a peer's words gives up after the communicator's peer timeout
+// (2 s unless set) and flags DEV_TIMEOUT_PEER in the workspace status word.
+// The launch that gave up still counts its epoch, while a rank that never
+// made the call does not, so after such a failure the ranks' epochs differ
+// for good: wr_comm_reset on every rank (between two host barriers) puts
+// them back in step.
 //
 // warp-route is single-GPU; this replaces the separate NCCL all-reduce a
 // tensor- or expert-parallel caller would run after each layer.
@@ -26,6 +33,7 @@
 
 struct wr_comm {
   int rank = 0, world = 1, H = 0, device = 0;
+  uint64_t peer_wait_ns = wr::kPeerWaitDefaultNs;
   void* local = nullptr;
   size_t bytes = 0;
   cudaIpcMemHandle_t handle{};
@@ -59,6 +67,7 @@ wr_status_t comm_view(const wr_comm* c, CommView* v) {
   v->rank = c->rank;
   v->world = c->world;
   v->H = c->H;
+  v->peer_wait_ns = c->peer_wait_ns;
   return WR_OK;
 }
 
@@ -124,6 +133,28 @@ wr_status_t wr_comm_open(wr_comm_t comm, const void* handles) {
     comm->peers[q] = p;
   }
   comm->open = true;
+  return WR_OK;
+}
+
+wr_status_t wr_comm_set_peer_timeout_ns(wr_comm_t comm, uint64_t ns) {
+  if (!comm) return fail(WR_ERR_INVALID, "comm must not be NULL");
+  comm->peer_wait_ns = ns ? ns : kPeerWaitDefaultNs;
+  return WR_OK;
+}
+
+wr_status_t wr_comm_reset(wr_comm_t comm, wr_stream_t stream) {
+  if (!comm) return fail(WR_ERR_INVALID, "comm must not be NULL");
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != comm->device)
+    return fail(WR_ERR_COMM, "communicator belongs to device %d, current device is %d",
+                comm->device, dev);
+  // Epoch 0 and an all-zero mailbox: no launch uses epoch 0, so no word left
+  // over from before the reset can pass for a new launch's.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(comm->local, 0, comm->bytes, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "wr_comm_reset");
   return WR_OK;
 }
 

@@ -142,7 +142,7 @@ struct FusedArgs {
   int ep_first, ep_num;
   Layout lay;
   Plan pl;
-  CommView comm;  // comm.world == 1: no all-reduce
+  CommView comm;  // comm.world == 0: no all-reduce (a one-rank communicator still runs it)
 };
 
 WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts; }
@@ -452,12 +452,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   griddep_wait();
   griddep_launch_dependents();
   uint32_t* s_epoch = reinterpret_cast<uint32_t*>(misc + kOffEpoch);
-  if (tid == 0 && a.comm.world > 1) *s_epoch = *a.comm.epoch + 1;  // read after the previous launch
+  if (tid == 0 && a.comm.world > 0) *s_epoch = *a.comm.epoch + 1;  // read after the previous launch
   // Output value v of token t, row h: into `out`, or with an all-reduce as
   // the word (v | epoch << 32) into this rank's slot of every rank's
   // mailbox (*s_epoch is read after the __syncthreads below, before use).
   auto emit = [&](int t, int h, float v) {
-    if (a.comm.world > 1) {
+    if (a.comm.world > 0) {
       const uint32_t e = *s_epoch;
       const uint64_t word = ((uint64_t)e << 32) | __float_as_uint(v);
       const size_t off =
@@ -914,7 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       named_bar_sync(kBarConsumers, kConsumerThreads);  // all row accumulators final
       // (with an all-reduce the rows are written even after a failed wait,
       // so the peers' waits end; the status word reports the failure)
-      if ((ok && !*abort_flag) || a.comm.world > 1) {
+      if ((ok && !*abort_flag) || a.comm.world > 0) {
         for (int idx = tid; idx < T * nb; idx += kConsumerThreads) {
           const int t = idx / nb;
           const int h = idx - t * nb;
@@ -934,7 +934,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   }
 
   __syncthreads();
-  if (a.comm.world > 1) {
+  if (a.comm.world > 0) {
     // ---- one-shot all-reduce: this CTA's rows of every rank ----
     // Each word of this rank's mailbox is polled until it carries this
     // launch's epoch; the values are summed in source-rank order.
@@ -950,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
             a.comm.box[a.comm.rank] + (((size_t)q * 2 + (e & 1u)) * kCommMaxTokens + t) * H + h;
         uint64_t w = ld_relaxed_sys_u64(p);
         for (uint32_t spin = 1; (uint32_t)(w >> 32) != e && !late; ++spin) {
-          if ((spin & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          if ((spin & 63u) == 0 && globaltimer_ns() - t0 > a.comm.peer_wait_ns) {
             atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_PEER);
             late = true;
           }
@@ -969,7 +969,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     if (prev == (uint32_t)G - 1) {
       for (int s = 0; s < S; ++s) atomicExch(&a.sync[kSyncSlot0 + s], 0u);
       atomicExch(&a.sync[kSyncRouter], 0u);
-      if (a.comm.world > 1) *a.comm.epoch = *s_epoch;  // the next launch uses epoch + 1
+      if (a.comm.world > 0) *a.comm.epoch = *s_epoch;  // the next launch uses epoch + 1
       atomicExch(&a.sync[kSyncExit], 0u);
       __threadfence();
     }
@@ -1120,8 +1120,7 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
   if (comm) {
     args.comm = *comm;
   } else {
-    args.comm = CommView{};
-    args.comm.world = 1;
+    args.comm = CommView{};  // world 0: no all-reduce
   }
   args.x = x;
   args.wbuf = static_cast<const uint8_t*>(wbuf);

@@ -672,7 +672,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
       for (int c = 0; c < 4; ++c) {
         uint64_t wv = ld_relaxed_sys_u64(p + c);
         for (uint32_t spin = 1; (uint32_t)(wv >> 32) != ep && !late; ++spin) {
-          if ((spin & 63u) == 0 && globaltimer_ns() - tstart > kWaitLimitNs) {
+          if ((spin & 63u) == 0 && globaltimer_ns() - tstart > comm.peer_wait_ns) {
             atomicOr(ctl + 2, DEV_TIMEOUT_PEER);
             late = true;
           }

@@ -28,7 +28,11 @@ struct CommView {
   uint64_t* box[kMaxRanks];
   uint32_t* epoch;
   int rank, world, H;
+  uint64_t peer_wait_ns;  // bound of each wait for a peer's words (ns)
 };
+
+// Default bound of a wait for a peer rank's partial outputs (ns).
+constexpr uint64_t kPeerWaitDefaultNs = 2000000000ull;
 
 // The kernel's view of an open communicator on the current device.
 wr_status_t comm_view(const wr_comm* c, CommView* v);

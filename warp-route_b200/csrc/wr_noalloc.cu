@@ -17,10 +17,13 @@
 //     DBRX and DeepSeek shapes fit); larger shapes are rejected with
 //     WR_ERR_UNSUPPORTED before anything is launched;
 //   * all calls on a device share the one array, which keeps the last call's
-//     contents: the control words that must start at zero are cleared on the
+//     contents: the counters that must start at zero are cleared on the
 //     caller's stream before every launch, and calls that overlap on the GPU
 //     (several streams, several host threads) race on the array — serialise
 //     them;
+//   * the status word (set when a bounded wait inside a kernel gave up) is
+//     not cleared by a call: wr_fused_moe_noalloc_status reads and clears
+//     it, as wr_workspace_status does for a caller's workspace;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current) and caches it; make
 //     that first call before any stream capture begins.
@@ -35,7 +38,8 @@ namespace wr {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 1u << 20;
-constexpr size_t kControlBytes = kWsControlBytes;  // counters and status word, must start at zero
+constexpr size_t kControlBytes = kWsControlBytes;  // counters and the status word
+constexpr size_t kStatusOffset = 8;                // the status word (32-bit word 2)
 
 // The shared scratch.  Host code must not use this name as a device address:
 // on the host it denotes a host-side stand-in.  Its device address comes from
@@ -97,9 +101,21 @@ extern "C" wr_status_t wr_fused_moe_noalloc(const wr_moe_desc_t* desc, const voi
   void* scratch = nullptr;
   wr_status_t st = scratch_address(&scratch);
   if (st != WR_OK) return st;
-  cudaError_t e =
-      cudaMemsetAsync(scratch, 0, kControlBytes, static_cast<cudaStream_t>(stream));
+  // Every control word but the status word, which keeps a failed wait's bits
+  // until wr_fused_moe_noalloc_status reads them.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ctl = static_cast<uint8_t*>(scratch);
+  cudaError_t e = cudaMemsetAsync(ctl, 0, kStatusOffset, s);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(ctl + kStatusOffset + 4, 0, kControlBytes - kStatusOffset - 4, s);
   if (e != cudaSuccess) return cuda_fail(e, "wr_fused_moe_noalloc: clearing the control words");
   return wr_fused_moe(desc, x, gate_w, weight_buf, weight_buf_bytes, out, topk_ids, topk_weights,
                       scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" wr_status_t wr_fused_moe_noalloc_status(wr_stream_t stream) {
+  void* scratch = nullptr;
+  wr_status_t st = scratch_address(&scratch);
+  if (st != WR_OK) return st;
+  return wr_workspace_status(scratch, stream);
 }

@@ -12,6 +12,7 @@ import torch
 import torch.nn as nn
 
 from .functional import (
+    _expert_stride_elems,
     _pack_expert_weights,
     batched_fused_moe,
     fused_moe,
@@ -43,9 +44,18 @@ class MoELayer(nn.Module):
     up_proj / down_proj, N(0, 0.02) init, forward on [H] (one token) or
     [B, H] (a decode batch).  Differences: top_k may be any value in
     [1, num_experts]; `dtype` selects float32 (default) or bfloat16
-    parameters; the packed weight buffer is cached and rebuilt only when a
-    parameter changes (warp-route repacks every expert on every forward);
-    the output is float32.
+    parameters; the output is float32; and the expert parameters are views
+    into one packed [gate | up | down] buffer in the kernels' layout, so a
+    forward hands that buffer to the kernel as it is (warp-route repacks
+    every expert on every forward, warp_route/__init__.py:81).
+
+    Because the parameters share the buffer's memory, every in-place write —
+    `p.copy_(w)`, `p.data.copy_(w)`, an optimizer step, `load_state_dict` —
+    is the packed buffer's content at once; nothing can go stale.  When a
+    parameter stops being such a view (`module.to(...)`, `.cuda()`,
+    `.bfloat16()`, assigning a new tensor to `p.data` or a new Parameter),
+    the next forward repacks the parameters into a new buffer on their
+    device and makes them views of it again.
     """
 
     def __init__(
@@ -66,18 +76,15 @@ class MoELayer(nn.Module):
         self.intermediate_dim = intermediate_dim
         self.top_k = top_k
 
-        self.router = nn.Parameter(torch.empty(num_experts, hidden_dim, dtype=dtype))
-        self.gate_proj = nn.ParameterList(
-            [nn.Parameter(torch.empty(intermediate_dim, hidden_dim, dtype=dtype))
-             for _ in range(num_experts)])
-        self.up_proj = nn.ParameterList(
-            [nn.Parameter(torch.empty(intermediate_dim, hidden_dim, dtype=dtype))
-             for _ in range(num_experts)])
-        self.down_proj = nn.ParameterList(
-            [nn.Parameter(torch.empty(hidden_dim, intermediate_dim, dtype=dtype))
-             for _ in range(num_experts)])
-        self._packed: Optional[torch.Tensor] = None
-        self._packed_key = None
+        E, H, I = num_experts, hidden_dim, intermediate_dim
+        self.router = nn.Parameter(torch.empty(E, H, dtype=dtype))
+        buf = torch.zeros(E * _expert_stride_elems(H, I, torch.empty((), dtype=dtype).element_size()),
+                          dtype=dtype)
+        views = self._views(buf)
+        self.gate_proj = nn.ParameterList([nn.Parameter(g) for g, _, _ in views])
+        self.up_proj = nn.ParameterList([nn.Parameter(u) for _, u, _ in views])
+        self.down_proj = nn.ParameterList([nn.Parameter(d) for _, _, d in views])
+        self._packed: torch.Tensor = buf
         self._init_weights()
 
     def _init_weights(self) -> None:
@@ -86,21 +93,48 @@ class MoELayer(nn.Module):
             nn.init.normal_(self.gate_proj[e], std=0.02)
             nn.init.normal_(self.up_proj[e], std=0.02)
             nn.init.normal_(self.down_proj[e], std=0.02)
-        self._packed = None
+
+    def _views(self, buf: torch.Tensor):
+        """Per expert, the (gate [I,H], up [I,H], down [H,I]) views of a
+        packed buffer (src/expert_layout.cuh:34-47 of warp-route)."""
+        H, I = self.hidden_dim, self.intermediate_dim
+        stride = _expert_stride_elems(H, I, buf.element_size())
+        n = I * H
+        out = []
+        for e in range(self.num_experts):
+            b = e * stride
+            out.append((buf[b:b + n].view(I, H), buf[b + n:b + 2 * n].view(I, H),
+                        buf[b + 2 * n:b + 3 * n].view(H, I)))
+        return out
 
     def _params(self):
         return list(self.gate_proj) + list(self.up_proj) + list(self.down_proj)
 
+    def _is_packed_view(self) -> bool:
+        """Every expert parameter is still the view of the packed buffer at
+        its own place (same memory, dtype and device)."""
+        buf = self._packed
+        for (g, u, d), pg, pu, pd in zip(self._views(buf), self.gate_proj, self.up_proj,
+                                         self.down_proj):
+            for v, p in ((g, pg), (u, pu), (d, pd)):
+                if (p.data_ptr() != v.data_ptr() or p.dtype != buf.dtype
+                        or p.device != buf.device or p.shape != v.shape):
+                    return False
+        return True
+
     def _pack_weights(self) -> torch.Tensor:
-        """Packed [gate|up|down] buffer, rebuilt only when a parameter's
-        storage or version counter changed since the last pack."""
-        key = tuple((p.data_ptr(), p._version, p.device, p.dtype) for p in self._params())
-        if self._packed is None or key != self._packed_key:
-            self._packed = _pack_expert_weights(
+        """The packed [gate|up|down] buffer the kernels read.  It is the
+        parameters' own memory; it is rebuilt (and the parameters re-pointed
+        at it) only when a parameter no longer lives in it."""
+        if not self._is_packed_view():
+            buf = _pack_expert_weights(
                 [p.data for p in self.gate_proj], [p.data for p in self.up_proj],
                 [p.data for p in self.down_proj], self.num_experts, self.hidden_dim,
                 self.intermediate_dim)
-            self._packed_key = key
+            for (g, u, d), pg, pu, pd in zip(self._views(buf), self.gate_proj, self.up_proj,
+                                             self.down_proj):
+                pg.data, pu.data, pd.data = g, u, d
+            self._packed = buf
         return self._packed
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

@@ -1,7 +1,7 @@
 """ctypes view of the C ABI in include/warp_route_b200.h.
 
-This is the binding a non-torch caller would write; the
-tests use it to drive the kernels through the exact C entry points.  Loading
+This is the binding a non-torch caller would write; the tests use it to
+drive the kernels through the exact C entry points.  Loading
 fails loudly when libwarp_route_b200.so is missing — there is no fallback.
 """
 from __future__ import annotations
@@ -62,6 +62,7 @@ SIGNATURES = {
     "wr_fused_moe_workspace_size": (_sz, [_D, _i32]),
     "wr_fused_moe": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "wr_fused_moe_noalloc": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "wr_fused_moe_noalloc_status": (_i32, [_vp]),
     "wr_batched_fused_moe": (_i32, [_D, _i32, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "wr_naive_moe_workspace_size": (_sz, [_D]),
     "wr_naive_moe": (_i32, [_D, _vp, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
@@ -74,6 +75,8 @@ SIGNATURES = {
     "wr_comm_get_handle": (_i32, [_vp, _vp]),
     "wr_comm_open": (_i32, [_vp, _vp]),
     "wr_comm_destroy": (_i32, [_vp]),
+    "wr_comm_set_peer_timeout_ns": (_i32, [_vp, ctypes.c_uint64]),
+    "wr_comm_reset": (_i32, [_vp, _vp]),
     "wr_fused_moe_allreduce": (_i32, [_D, _i32, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp,
                                       _vp]),
 }

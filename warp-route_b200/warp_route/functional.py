@@ -281,6 +281,24 @@ class PeerComm:
             raise RuntimeError("communicator is closed")
         return self._ptr
 
+    def set_peer_timeout(self, seconds: float) -> None:
+        """Bound of each wait for another rank's partial outputs (default
+        2 s; 0 restores it).  A call whose wait gives up returns a wrong
+        output and leaves WR_ERR_TIMEOUT in its workspace status."""
+        _load_extension().comm_set_peer_timeout_ns(self.handle, int(seconds * 1e9))
+
+    def reset(self, group=None) -> None:
+        """Recovery after a call timed out on any rank (collective over
+        `group`): once no rank has a layer call in flight, every rank puts its
+        launch counter and mailbox back to zero, between two barriers, so the
+        ranks' launches are numbered alike again."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group)
+        _load_extension().comm_reset(self.handle)
+        dist.barrier(group)
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (call on every
         rank, after the last layer call has finished)."""
@@ -302,13 +320,17 @@ def fused_moe_allreduce(
     router_bias: Optional[torch.Tensor] = None,
     ep_first_expert: int = 0,
     ep_num_local: int = 0,
-) -> torch.Tensor:
+    return_routing: bool = False,
+):
     """This rank's shard of the layer with every rank's output summed in the
     same kernel: x [H] or [T,H] -> float32, the full layer output on every
     rank.  weight_buf holds this rank's shard: a tensor-parallel slice
     (intermediate_dim = this rank's columns) or, with ep_num_local > 0, the
-    experts [ep_first_expert, ep_first_expert + ep_num_local)."""
+    experts [ep_first_expert, ep_first_expert + ep_num_local).  With
+    return_routing=True the result is (out, expert ids int32 [T,K], weights
+    fp32 [T,K]), the routing being identical on every rank."""
     _C = _load_extension()
-    return _C.fused_moe_allreduce(x, gate_w, weight_buf, num_experts, hidden_dim,
-                                  intermediate_dim, top_k, comm.handle, router_bias,
-                                  ep_first_expert, ep_num_local)[0]
+    res = _C.fused_moe_allreduce(x, gate_w, weight_buf, num_experts, hidden_dim,
+                                 intermediate_dim, top_k, comm.handle, router_bias,
+                                 ep_first_expert, ep_num_local)
+    return res if return_routing else res[0]
