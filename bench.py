@@ -91,6 +91,10 @@ def parse():
     ap.add_argument("--extra-configs", default="deepseek,dbrx",
                     help="other BASELINE configurations measured in the same run (expert "
                          "parallel at N > 1), reported under other_configs; empty: none")
+    ap.add_argument("--decode-layers", type=int, default=32,
+                    help="layers of the timed decode step (Mixtral shape, one token, tensor "
+                         "parallel at N > 1); 0: no decode step")
+    ap.add_argument("--decode-steps", type=int, default=5)
     ap.add_argument("--only-sweep", action="store_true",
                     help="run only the batched-decode sweep (N = 1) and print its JSON line")
     return ap.parse_args()
@@ -423,6 +427,86 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
                     "over ranks); hbm_gbs = distinct selected experts' weight bytes / time; "
                     "frac_of_hbm_peak = hbm_gbs / (N x measured HBM bandwidth)",
             "results": results}
+
+
+def decode_step(args, dev, world=1, rank=0):
+    """A 32-layer decode step (Mixtral shape, one token, tensor parallel over
+    the N GPUs with the ranks' sum fused into each layer kernel): the layers
+    chained with their residual connection, h <- (h + moe(h)).to(bf16), one
+    CUDA-graph replay per step.  `us_per_step` uses moe_decode_layer (the
+    residual and the next input written by the layer's own last step, one
+    kernel per layer); `unfused_us_per_step` the same stack with the residual
+    added by separate kernels after each layer (and, at N > 1, an NCCL
+    all-reduce instead of the fused sum).  The graph output is checked equal,
+    bit for bit, to the stack run eagerly."""
+    import torch.distributed as dist
+
+    from warp_route import functional as F
+    from warp_route import synthetic
+    from warp_route.decode import MoEStack, StackLayer
+
+    nl = args.decode_layers
+    if nl <= 0:
+        return None
+    E, H, I, K = SHAPES["mixtral"]
+    tp = world
+    layers = []
+    for li in range(nl):
+        L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, device=dev, seed=300 + li,
+                                 layer=li, tp_rank=rank, tp_size=tp)
+        layers.append(StackLayer(L.gate_w, L.weight_buf))
+    comm = F.PeerComm(H) if world > 1 else None
+    fused = MoEStack(layers, E, H, I // tp, K, 1, comm=comm)
+    unfused = MoEStack(layers, E, H, I // tp, K, 1,
+                       all_reduce=(dist.all_reduce if world > 1 else (lambda t: None)))
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(4242)
+    x = torch.randn(H, generator=gx, device=dev).to(torch.bfloat16)
+    res = {"layers": nl, "tokens": 1,
+           "parallelism": (f"tp{world}, ranks' sum fused into each layer kernel" if world > 1
+                           else "single GPU")}
+    rv_buf = torch.zeros(1, device=dev)
+    stream = torch.cuda.current_stream()
+    for name, stack in (("us_per_step", fused), ("unfused_us_per_step", unfused)):
+        ref = stack.eager(x)
+        got = stack.step(x).clone()
+        for _ in range(2):
+            stack.step(x)
+        torch.cuda.synchronize()
+        if name == "us_per_step":
+            res["graph_equals_eager"] = bool(torch.equal(got, ref))
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clk:
+            start_together(world, stream, lambda: dist.all_reduce(rv_buf))
+            t0.record(stream)
+            for _ in range(args.decode_steps):
+                stack.graph.replay()
+            t1.record(stream)
+            torch.cuda.synchronize()
+        tt = torch.tensor([t0.elapsed_time(t1)], device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        res[name] = round(tt.item() * 1000.0 / args.decode_steps, 2)
+        if name == "us_per_step":
+            res["us_per_layer"] = round(res[name] / nl, 3)
+            res["clocks"] = clk.summary()
+        stack.close()
+    st = torch.tensor([F._load_extension().workspace_status(x)], device=dev)
+    with torch.cuda.stream(fused.stream):
+        st = st + F._load_extension().workspace_status(x)
+    if world > 1:
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+    if st.item() != 0:
+        raise SystemExit(f"decode step: device status {st.item()}: timing discarded")
+    if comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+    del fused, unfused, layers
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    res["steps"] = args.decode_steps
+    return res
 
 
 # The GPU stays busy this long (≈ 2 ms at up to 2 GHz) while the host
@@ -848,6 +932,8 @@ def run_ours(args, world, rank, local):
             dist.barrier()
             comm.close()
 
+    dec = decode_step(args, dev, world, rank)
+
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -865,6 +951,8 @@ def run_ours(args, world, rank, local):
             line["other_configs"] = extras
         if sweep is not None:
             line["batched_sweep"] = sweep
+        if dec is not None:
+            line["decode_step"] = dec
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

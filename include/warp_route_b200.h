@@ -234,6 +234,29 @@ WR_API wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num
                                           void* workspace, size_t workspace_bytes,
                                           wr_comm_t comm, wr_stream_t stream);
 
+/* ---- one layer of a decode stack --------------------------------------- */
+
+/* The layer with the residual connection of a decode stack fused into its
+ * last step: out = x + layer(x) in fp32 (with comm: the sum over the ranks'
+ * shards first, exactly as wr_fused_moe_allreduce), and, when next_x is not
+ * NULL, next_x = out rounded to desc->dtype (round to nearest even): the
+ * next layer's input, written by the same kernel.  This is the arithmetic of
+ * `h = (h.float() + layer(h)).to(dtype)`, bit for bit, without the two extra
+ * kernels a plain decode loop launches per layer.  x [T,H] and next_x [T,H]
+ * in desc->dtype (next_x must not alias x), out [T,H] fp32, the other
+ * arguments as wr_batched_fused_moe; comm may be NULL (one GPU).  Shapes
+ * that only the multi-kernel path takes (misaligned pointers, H or I not a
+ * multiple of 16 bytes of elements) get WR_ERR_UNSUPPORTED.  No warp-route
+ * counterpart: warp-route runs one layer per call and leaves the residual to
+ * the caller (the per-layer launch overhead its README.md:17 cites). */
+WR_API wr_status_t wr_moe_decode_layer(const wr_moe_desc_t* desc, int32_t num_tokens,
+                                       const void* x, const void* gate_w,
+                                       const void* weight_buf, int64_t weight_buf_bytes,
+                                       float* out, void* next_x, int32_t* topk_ids,
+                                       float* topk_weights, void* workspace,
+                                       size_t workspace_bytes, wr_comm_t comm,
+                                       wr_stream_t stream);
+
 /* ---- weight packing ---------------------------------------------------- */
 
 /* Packs one rank's shard of the expert weights into the flat layout (see

@@ -71,6 +71,7 @@ wr_status_t make_problem(const wr_moe_desc_t* d, int tokens, Problem* p) {
   p->dtype = d->dtype;
   p->elt = d->dtype == WR_DTYPE_BF16 ? 2 : 4;
   p->router_bias = d->router_bias;
+  p->res = Residual{nullptr, nullptr, d->dtype == WR_DTYPE_BF16 ? 1 : 0};
   if (d->ep_num_local == 0) {
     p->ep_first = 0;
     p->ep_num = p->E;
@@ -142,6 +143,10 @@ wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const
     float* oq = out + (size_t)t0 * p.H;
     int32_t* iq = ids ? ids + (size_t)t0 * p.K : nullptr;
     float* wq = w ? w + (size_t)t0 * p.K : nullptr;
+    if (p.res.x) {  // this block's rows of x and next_x
+      q.res.x = xq;
+      q.res.next_x = p.res.next_x ? static_cast<uint8_t*>(p.res.next_x) + xoff : nullptr;
+    }
     wr_status_t st;
     if (ptr_ok && aligned16(xq) && fused_supported(q))
       st = launch_fused(q, xq, gate_w, wbuf, oq, iq, wq, ws, stream, comm);
@@ -149,6 +154,10 @@ wr_status_t run_layer(const Problem& p, const void* x, const void* gate_w, const
       st = fail(WR_ERR_UNSUPPORTED,
                 "the all-reduce layer needs the streaming kernel: 16-byte aligned x, gate_w and "
                 "weight_buf, and H, I multiples of 16 bytes of elements");
+    else if (p.res.x)
+      st = fail(WR_ERR_UNSUPPORTED,
+                "the fused residual needs the streaming or grouped kernels: 16-byte aligned x, "
+                "gate_w and weight_buf, and H, I multiples of 16 bytes of elements");
     else
       st = launch_naive(q, xq, gate_w, wbuf, oq, iq, wq, ws, stream);
     if (st != WR_OK) return st;
@@ -269,6 +278,31 @@ wr_status_t wr_fused_moe_allreduce(const wr_moe_desc_t* desc, int32_t num_tokens
   if ((st = check_ws(workspace, workspace_bytes, fused_ws_for(p))) != WR_OK) return st;
   return run_layer(p, x, gate_w, weight_buf, out, topk_ids, topk_weights, workspace,
                    static_cast<cudaStream_t>(stream), &v);
+}
+
+wr_status_t wr_moe_decode_layer(const wr_moe_desc_t* desc, int32_t num_tokens, const void* x,
+                                const void* gate_w, const void* weight_buf,
+                                int64_t weight_buf_bytes, float* out, void* next_x,
+                                int32_t* topk_ids, float* topk_weights, void* workspace,
+                                size_t workspace_bytes, wr_comm_t comm, wr_stream_t stream) {
+  Problem p;
+  wr_status_t st = make_problem(desc, num_tokens, &p);
+  if (st != WR_OK) return st;
+  if (num_tokens == 0) return WR_OK;
+  if (!x || !gate_w || !out) return fail(WR_ERR_INVALID, "x, gate_w and out must not be NULL");
+  if (next_x == x) return fail(WR_ERR_INVALID, "next_x must not alias x");
+  if ((st = check_weights(p, weight_buf, weight_buf_bytes)) != WR_OK) return st;
+  if ((st = check_ws(workspace, workspace_bytes, fused_ws_for(p))) != WR_OK) return st;
+  CommView v;
+  if (comm) {
+    if ((st = comm_view(comm, &v)) != WR_OK) return st;
+    if (v.H != p.H)
+      return fail(WR_ERR_INVALID, "hidden_dim %d differs from the communicator's %d", p.H, v.H);
+  }
+  p.res.x = x;
+  p.res.next_x = next_x;
+  return run_layer(p, x, gate_w, weight_buf, out, topk_ids, topk_weights, workspace,
+                   static_cast<cudaStream_t>(stream), comm ? &v : nullptr);
 }
 
 size_t wr_naive_moe_workspace_size(const wr_moe_desc_t* desc) {

@@ -307,6 +307,53 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_moe_allreduce(
                     reinterpret_cast<wr_comm_t>(comm));
 }
 
+// One layer of a decode stack with the residual fused (wr_moe_decode_layer):
+// returns out = hidden + layer(hidden) (fp32, summed over the ranks when comm
+// is given) and writes next_x = out in hidden's dtype when next_x is given.
+torch::Tensor moe_decode_layer(torch::Tensor hidden, torch::Tensor gate_w,
+                               torch::Tensor weight_buf, int num_experts, int hidden_dim,
+                               int intermediate_dim, int top_k, int64_t comm,
+                               c10::optional<torch::Tensor> router_bias, int ep_first_expert,
+                               int ep_num_local, c10::optional<torch::Tensor> next_x) {
+  CHECK_CUDA(hidden);
+  CHECK_CONTIGUOUS(hidden);
+  CHECK_DTYPE(hidden);
+  TORCH_CHECK((hidden.dim() == 1 && hidden.size(0) == hidden_dim) ||
+                  (hidden.dim() == 2 && hidden.size(1) == hidden_dim),
+              "hidden must have shape [", hidden_dim, "] or [batch_size, ", hidden_dim,
+              "], got shape ", hidden.sizes());
+  validate_2d(gate_w, "gate_w", num_experts, hidden_dim);
+  check_same(hidden, gate_w, "hidden", "gate_w");
+  check_weight_buf(hidden, weight_buf);
+  void* nx = nullptr;
+  if (next_x.has_value() && next_x->defined()) {
+    const auto& n = *next_x;
+    CHECK_CUDA(n);
+    CHECK_CONTIGUOUS(n);
+    check_same(hidden, n, "hidden", "next_x");
+    TORCH_CHECK(n.sizes() == hidden.sizes(), "next_x must have hidden's shape ", hidden.sizes(),
+                ", got ", n.sizes());
+    nx = n.data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(hidden.device().index()).stream();
+  wr_moe_desc_t d = make_desc(hidden, num_experts, hidden_dim, intermediate_dim, top_k,
+                              router_bias, ep_first_expert, ep_num_local);
+  const int64_t T = hidden.dim() == 1 ? 1 : hidden.size(0);
+  auto fopt = torch::TensorOptions().dtype(torch::kFloat32).device(hidden.device());
+  torch::Tensor out = torch::empty(hidden.sizes(), fopt);
+  if (T == 0) return out;
+  const size_t need = wr_fused_moe_workspace_size(&d, (int32_t)T);
+  TORCH_CHECK(need > 0, wr_last_error_string());
+  torch::Tensor ws = workspace_for(hidden.device(), stream, need);
+  check_status(wr_moe_decode_layer(&d, (int32_t)T, hidden.data_ptr(), gate_w.data_ptr(),
+                                   weight_buf.data_ptr(),
+                                   weight_buf.numel() * (int64_t)weight_buf.element_size(),
+                                   out.data_ptr<float>(), nx, nullptr, nullptr, ws.data_ptr(),
+                                   (size_t)ws.numel(), reinterpret_cast<wr_comm_t>(comm), stream));
+  return out;
+}
+
 // One rank's shard of per-expert weight lists packed on the device
 // (wr_pack_experts): experts [ep_first, ep_first + ep_num), intermediate
 // slice tp_rank of tp_size.  Entries outside the shard are not read.
@@ -399,6 +446,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("hidden_dim"), py::arg("intermediate_dim"), py::arg("top_k"), py::arg("comm"),
         py::arg("router_bias") = py::none(), py::arg("ep_first_expert") = 0,
         py::arg("ep_num_local") = 0);
+  m.def("moe_decode_layer", &moe_decode_layer,
+        "Layer with the residual fused: out = hidden + layer(hidden); next_x = out in the "
+        "layer dtype",
+        py::arg("hidden"), py::arg("gate_w"), py::arg("weight_buf"), py::arg("num_experts"),
+        py::arg("hidden_dim"), py::arg("intermediate_dim"), py::arg("top_k"), py::arg("comm"),
+        py::arg("router_bias") = py::none(), py::arg("ep_first_expert") = 0,
+        py::arg("ep_num_local") = 0, py::arg("next_x") = py::none());
   m.def("pack_experts", &pack_experts,
         "Pack one rank's shard (experts, intermediate slice) of per-expert weights on the "
         "device");

@@ -3,6 +3,7 @@
 // bf16 unpacking and the packed expert layout.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -83,6 +84,21 @@ WR_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe: has the phase with `parity` completed?  (try_wait may
+// suspend the thread for a while when the phase is still open; a loop that
+// polls several conditions uses this instead.)
+WR_DEVINL bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -226,6 +242,24 @@ WR_DEVINL float load_scalar<float>(const float* p, int64_t i) {
 }
 
 WR_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// Layer output element i (of [T, H]) with the fused residual connection:
+// returns v + x[i] and, when next_x is set, stores that sum rounded to the
+// layer dtype (round to nearest even) as next_x[i].  x == null: v as is.
+template <typename Res>
+WR_DEVINL float residual_out(const Res& r, int64_t i, float v) {
+  if (!r.x) return v;
+  float o;
+  if (r.bf16) {
+    o = v + __uint_as_float((uint32_t)static_cast<const uint16_t*>(r.x)[i] << 16);
+    if (r.next_x)
+      static_cast<uint16_t*>(r.next_x)[i] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+  } else {
+    o = v + static_cast<const float*>(r.x)[i];
+    if (r.next_x) static_cast<float*>(r.next_x)[i] = o;
+  }
+  return o;
+}
 
 // Programmatic dependent launch: wait for the previous kernel on the stream
 // (complete, memory visible) / let the next one be scheduled.  Both are

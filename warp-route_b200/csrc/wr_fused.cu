@@ -81,7 +81,7 @@ constexpr int kVecMaxBytes = kMiscOff - 4 * kMaxStageBytes;  // x / activation w
 static_assert(kVecMaxBytes % 64 == 0, "vector region must keep 64-byte alignment");
 
 // Offsets inside the misc region (at the end of shared memory).
-constexpr int kOffBars = 0;        // full[12], empty[12], act
+constexpr int kOffBars = 0;        // full[12], empty[12]
 constexpr int kOffAbort = 256;     // int
 constexpr int kOffNSlots = 260;    // int
 constexpr int kOffSlotTag = 264;   // int [12]: stage number each ring slot currently holds
@@ -92,7 +92,11 @@ constexpr int kOffTokIds = 1792;   // int [NT * 64]
 constexpr int kOffTokW = 2816;     // float [NT * 64]
 constexpr int kOffSlotBar = 3840;  // mbarrier [64]: the W consumer warps are done with slot s
 constexpr int kOffLogits = 4352;   // float [NT * 64]: router logits
-static_assert(kOffBars + 8 * (2 * kMaxStages + 1) <= kOffAbort, "misc");
+constexpr int kMaxActBufs = 16;    // phase B: activation window buffers, at most
+constexpr int kOffActBars = 5376;  // mbarrier act_full[16], act_empty[16]
+static_assert(kOffBars + 8 * (2 * kMaxStages) <= kOffAbort, "misc");
+static_assert(kOffLogits + 4 * kMaxNT * kMaxExperts <= kOffActBars, "misc");
+static_assert(kOffActBars + 16 * kMaxActBufs <= kMiscBytes, "misc");
 static_assert(kOffTokW + 4 * kMaxNT * kMaxExperts <= kOffSlotBar, "misc");
 static_assert(kOffSlotBar + 8 * kMaxExperts <= kOffLogits, "misc");
 static_assert(kOffLogits + 4 * kMaxNT * kMaxExperts <= kMiscBytes, "misc");
@@ -125,6 +129,10 @@ struct Plan {
   int localR;  // router: every CTA computes all partial sums itself (small routers)
   int NBM;     // phase B: most output rows one CTA holds
   int RA;      // float offset of the per-warp row accumulators [W][NBM][NT] in the vector region
+  int AOFF;    // float offset of the activation window buffers in the vector region (0: they
+               // overlap x, so the first window may only land once phase A is over)
+  int CB;      // activation window buffers (1 .. kMaxActBufs)
+  int WBF;     // floats per activation window buffer (WB * NT, 64-byte multiple)
 };
 
 struct FusedArgs {
@@ -143,6 +151,7 @@ struct FusedArgs {
   Layout lay;
   Plan pl;
   CommView comm;  // comm.world == 0: no all-reduce (a one-rank communicator still runs it)
+  Residual res;   // res.x == null: out = layer(x); else out = x + layer(x) (+ next_x)
 };
 
 WR_DEVINL int64_t split_lo(int64_t n, int i, int parts) { return (n * i) / parts; }
@@ -409,7 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   uint8_t* misc = smem + kMiscOff;
   uint64_t* full = reinterpret_cast<uint64_t*>(misc + kOffBars);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* actbar = empty + kMaxStages;
+  uint64_t* act_full = reinterpret_cast<uint64_t*>(misc + kOffActBars);
+  uint64_t* act_empty = act_full + kMaxActBufs;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + kOffAbort);
   int* s_nslots = reinterpret_cast<int*>(misc + kOffNSlots);
   volatile int* slot_tag = reinterpret_cast<volatile int*>(misc + kOffSlotTag);
@@ -434,7 +444,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
       mbar_init(&empty[s], W);
       slot_tag[s] = -1;
     }
-    mbar_init(actbar, 1);
+    for (int q = 0; q < pl.CB; ++q) {
+      mbar_init(&act_full[q], 1);
+      mbar_init(&act_empty[q], W);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -464,7 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           (((size_t)a.comm.rank * 2 + (e & 1u)) * kCommMaxTokens + t) * (size_t)H + h;
       for (int q = 0; q < a.comm.world; ++q) st_relaxed_sys_u64(a.comm.box[q] + off, word);
     } else {
-      a.out[(int64_t)t * H + h] = v;
+      const int64_t i = (int64_t)t * H + h;
+      a.out[i] = residual_out(a.res, i, v);
     }
   };
 
@@ -680,20 +694,74 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     }
   } else if (warp == W + 1) {
     // =========================== publisher ==================================
-    // Once all W consumer warps of this CTA have written their slot-s
+    // (1) Once all W consumer warps of this CTA have written their slot-s
     // activations (each arrives on slot_bar[s], used once per launch), counts
     // the CTA in on the grid-wide counter of slot s with one GPU-scope
     // release, so the consumers never stall on a GPU-scope release.
+    // (2) Phase B's activation windows (slot s, window win; j = s * nwin +
+    // win) go into pl.CB buffers round robin: window j is copied into buffer
+    // j % CB as soon as slot s is complete grid-wide and the consumers have
+    // released the buffer's previous window (act_empty), so a slot's
+    // activations are in shared memory before its rows come up instead of
+    // each slot costing a grid-wide wait plus a copy in the consumers' path.
+    // With AOFF == 0 the buffers overlap x, and the first window waits for
+    // the end of phase A (every consumer warp has published every slot).
+    // Both jobs are polled in one loop, so neither waits behind the other.
     if (lane == 0) {
-      for (int s = 0; s < S; ++s) {
-        if (!mbar_wait(&slot_bar[s], 0u, abort_flag)) {
-          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
-          *abort_flag = 1;
-          break;
+      const int NW = S * pl.nwin;
+      const uint64_t pol = l2_policy_evict_last();
+      int pub = 0, win_j = 0;
+      uint64_t t_prog = globaltimer_ns();
+      uint32_t spins = 0;
+      bool ok = true;
+      while (ok && (pub < S || win_j < NW)) {
+        bool prog = false;
+        if (pub < S && mbar_test_wait(&slot_bar[pub], 0u)) {
+          fence_proxy_async_global();
+          red_release_gpu_add(&a.sync[kSyncSlot0 + pub], 1u);
+          ++pub;
+          prog = true;
         }
-        fence_proxy_async_global();
-        red_release_gpu_add(&a.sync[kSyncSlot0 + s], 1u);
+        if (win_j < NW) {
+          const int s = win_j / pl.nwin, win = win_j - s * pl.nwin;
+          const int ab = win_j % pl.CB;
+          const int use = win_j / pl.CB;
+          bool ready = use > 0 ? mbar_test_wait(&act_empty[ab], (uint32_t)(use - 1) & 1u)
+                               : (pl.AOFF > 0 || pub == S);
+          if (ready && win == 0) ready = ld_acquire_gpu(&a.sync[kSyncSlot0 + s]) >= (uint32_t)G;
+          if (ready) {
+            fence_proxy_async_global();  // the peers' activations, then async-proxy reads
+            if (use == 0) fence_proxy_async_smem();  // x or nothing was here (generic writes)
+            const int c0 = win * pl.WB;
+            const int wc = win + 1 < pl.nwin ? pl.WB : I - (pl.nwin - 1) * pl.WB;
+            const uint32_t bytes = (uint32_t)wc * NT * 4;
+            uint8_t* dst = reinterpret_cast<uint8_t*>(vreg + pl.AOFF + ab * pl.WBF);
+            const uint8_t* src =
+                reinterpret_cast<const uint8_t*>(a.act + ((int64_t)s * I + c0) * NT);
+            mbar_arrive_expect_tx(&act_full[ab], bytes);
+            for (uint32_t off = 0; off < bytes; off += 32768u)
+              bulk_g2s(dst + off, src + off, min(32768u, bytes - off), &act_full[ab], pol);
+            ++win_j;
+            prog = true;
+          }
+        }
+        if (prog) {
+          t_prog = globaltimer_ns();
+        } else if ((++spins & 63u) == 0) {
+          if (*abort_flag) {
+            ok = false;
+          } else if (globaltimer_ns() - t_prog > kWaitLimitNs) {
+            atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
+            *abort_flag = 1;
+            ok = false;
+          }
+        }
       }
+      // Every window copy issued lands before the CTA can exit (the
+      // consumers have waited for all of them unless the launch aborted).
+      for (int j = win_j > pl.CB ? win_j - pl.CB : 0; j < win_j; ++j)
+        if (!mbar_wait(&act_full[j % pl.CB], (uint32_t)(j / pl.CB) & 1u, nullptr))
+          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
     }
   } else {
     // =========================== consumer warps =============================
@@ -825,49 +893,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
 
     // ---- phase B: down rows, slot by slot.  Each row is read by PB warps,
     // each taking a column slice; warp w adds into its own accumulators
-    // rowacc[w][h][t], summed in warp order at the end. ----
+    // rowacc[w][h][t], summed in warp order at the end.  The activation
+    // window of (slot s, window win) is the j-th, in buffer j % CB; the
+    // publisher warp fills it, and each warp releases it after its rows. ----
     {
-      const uint32_t slot_target = (uint32_t)G;
       const int GW = W / pl.PB;         // row groups of PB warps
       const int partB = warp % pl.PB;   // my column slice
       const int grpB = warp / pl.PB;    // my row group
-      uint32_t aw = 0;
-      int act_issued = 0;
+      named_bar_sync(kBarConsumers, kConsumerThreads);  // row accumulators zeroed
+      int j = 0;
       for (int s = 0; s < S; ++s) {
-        for (int win = 0, c0 = 0; win < pl.nwin; ++win, c0 += pl.WB) {
+        for (int win = 0; win < pl.nwin; ++win, ++j) {
           const int wc = win + 1 < pl.nwin ? pl.WB : wc_last;
           const int nch = wc / VEC;
-          named_bar_sync(kBarConsumers, kConsumerThreads);  // previous window fully read
+          const int ab = j % pl.CB;
+          const uint32_t use = (uint32_t)(j / pl.CB);
           if (*abort_flag) ok = false;
-          if (tid == 0 && ok && win == 0) {
-            // Every CTA has published slot s.
-            const uint64_t t0 = globaltimer_ns();
-            uint32_t spins = 0;
-            while (ld_acquire_gpu(&a.sync[kSyncSlot0 + s]) < slot_target) {
-              if ((++spins & 63u) == 0 &&
-                  (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs)) {
-                atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_GRID);
-                *abort_flag = 1;
-                ok = false;
-                break;
-              }
-            }
-            fence_proxy_async_global();
-          }
-          if (tid == 0 && ok) {
-            fence_proxy_async_smem();
-            const uint32_t bytes = (uint32_t)wc * NT * 4;
-            const uint64_t pol = l2_policy_evict_last();
-            mbar_arrive_expect_tx(actbar, bytes);
-            const uint8_t* src =
-                reinterpret_cast<const uint8_t*>(a.act + ((int64_t)s * I + c0) * NT);
-            for (uint32_t off = 0; off < bytes; off += 32768u)
-              bulk_g2s(reinterpret_cast<uint8_t*>(vreg) + off, src + off, min(32768u, bytes - off),
-                       actbar, pol);
-            act_issued = (int)aw + 1;
-          }
-          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(actbar, aw & 1u, abort_flag));
-          ++aw;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&act_full[ab], use & 1u, abort_flag));
+          const float* av = vreg + pl.AOFF + ab * pl.WBF;
           int hb = hb_start;
           for (int uu = 0; uu < nb_u; ++uu) {
             const int g = min(pl.GB, hb1 - hb);
@@ -886,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
                 for (int t = 0; t < NT; ++t) v[k][t] = 0.0f;
                 const int rr = first + k * GW;
                 if (rr < g)
-                  dot_down<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.WB * ELT), vreg, nch,
+                  dot_down<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.WB * ELT), av, nch,
                                    partB * 32 + lane, pl.PB * 32, v[k]);
               }
               __syncwarp();
@@ -908,6 +951,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
             hb += pl.GB;
             if (hb >= hb1) hb = hb0;
           }
+          // this warp is done with the window's buffer
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&act_empty[ab]);
           if (!ok && lane == 0) *abort_flag = 1;
         }
       }
@@ -923,11 +969,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
           for (int w = 1; w < W; ++w) o += rowacc[((int64_t)w * pl.NBM + h) * NT + t];
           emit(t, hb0 + h, o);
         }
-      }
-      if (tid == 0 && act_issued > 0 && !ok) {
-        // The last activation copy must land before the CTA exits.
-        if (!mbar_wait(actbar, (uint32_t)((act_issued - 1) & 1), nullptr))
-          atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_DRAIN);
       }
       if (lane == 0 && !ok) atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_FULL);
     }
@@ -958,7 +999,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
         }
         o += __uint_as_float((uint32_t)w);
       }
-      a.out[(int64_t)t * H + h] = o;
+      const int64_t i = (int64_t)t * H + h;
+      a.out[i] = residual_out(a.res, i, o);
     }
   }
   if (tid == 0) {
@@ -1072,13 +1114,42 @@ Plan make_plan(const Problem& p, int nt, int grid) {
   while (pl.PB > 1 && pl.GB > kRowsPerWarp * (kConsumerWarps / pl.PB)) pl.PB /= 2;
   pl.orderA = kOrderRoundRobin;
   pl.NBM = (p.H + grid - 1) / grid;
-  int64_t need = (int64_t)nt * p.H * 4;
-  if ((int64_t)pl.WB * nt * 4 > need) need = (int64_t)pl.WB * nt * 4;
-  need = (need + 63) / 64 * 64;
-  pl.RA = (int)(need / 4);
-  need += ((int64_t)kConsumerWarps * pl.NBM * nt * 4 + 63) / 64 * 64;
-  const int64_t nst = need < kMiscOff ? (kMiscOff - need) / sb : 0;
-  pl.nst = (int)(nst > kMaxStages ? kMaxStages : nst);
+  // The vector region holds x (bf16 as is, fp32 widened), the activation
+  // window buffers and the per-warp row accumulators; the ring gets the rest.
+  // Separate window buffers (after x) let the first windows land during
+  // phase A and later ones while earlier windows are read, but not at the
+  // cost of the weight stream: the ring keeps the stages the overlapped
+  // layout would have, up to 6 (6 x 32 KB in flight per SM covers HBM's
+  // latency).  Otherwise one window buffer shares x's space.
+  auto r64 = [](int64_t v) { return (v + 63) / 64 * 64; };
+  auto stages = [&](int64_t used) -> int64_t {
+    const int64_t n = used < kMiscOff ? (kMiscOff - used) / sb : 0;
+    return n > kMaxStages ? kMaxStages : n;
+  };
+  const int64_t xb = r64((int64_t)nt * p.H * (elt == 2 ? 2 : 4));
+  const int64_t winb = r64((int64_t)pl.WB * nt * 4);
+  const int64_t accb = r64((int64_t)kConsumerWarps * pl.NBM * nt * 4);
+  const int64_t ov = xb > winb ? xb : winb;
+  const int64_t nst_ov = stages(ov + accb);
+  const int64_t slots_max = p.ep_num < (int64_t)p.K * nt ? p.ep_num : (int64_t)p.K * nt;
+  int64_t nw_max = slots_max * pl.nwin;
+  if (nw_max > kMaxActBufs) nw_max = kMaxActBufs;
+  const int64_t keep = nst_ov < 6 ? nst_ov : 6;
+  int cb = 0;
+  for (int64_t q = nw_max; q >= 1 && cb == 0; --q)
+    if (stages(xb + q * winb + accb) >= (keep > 2 ? keep : 2)) cb = (int)q;
+  pl.WBF = (int)(winb / 4);
+  if (cb > 0) {
+    pl.AOFF = (int)(xb / 4);
+    pl.CB = cb;
+    pl.RA = (int)((xb + cb * winb) / 4);
+    pl.nst = (int)stages(xb + cb * winb + accb);
+  } else {
+    pl.AOFF = 0;
+    pl.CB = 1;
+    pl.RA = (int)(ov / 4);
+    pl.nst = (int)nst_ov;
+  }
   // Every CTA computes the whole router when it is small (<= 2 items per
   // consumer warp, <= 64 KB of router weights read from L2 by each CTA, the
   // partial sums fit in the ring); otherwise the items are spread over the grid.
@@ -1123,6 +1194,7 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w, co
     args.comm = CommView{};  // world 0: no all-reduce
   }
   args.x = x;
+  args.res = p.res;
   args.wbuf = static_cast<const uint8_t*>(wbuf);
   args.out = out;
   args.ids_out = ids;

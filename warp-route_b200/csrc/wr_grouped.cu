@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
                                                  const int4* __restrict__ row_tile,
                                                  const int* __restrict__ meta, int K, int H4,
                                                  int rmax, int kcB, int grid, int jmax,
-                                                 float4* __restrict__ out) {
+                                                 const Residual res, float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
@@ -596,6 +596,11 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
       acc.w += v.w;
     }
   }
+  const int64_t i = ((int64_t)t * H4 + h) * 4;
+  acc.x = residual_out(res, i + 0, acc.x);
+  acc.y = residual_out(res, i + 1, acc.y);
+  acc.z = residual_out(res, i + 2, acc.z);
+  acc.w = residual_out(res, i + 3, acc.w);
   out[(int64_t)t * H4 + h] = acc;
 }
 
@@ -618,6 +623,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
                                                     int rmax, int kcB, int grid, int jmax,
                                                     int t0,
                                                     int Tc, const CommView comm,
+                                                    const Residual res,
                                                     uint32_t* __restrict__ ctl,
                                                     float* __restrict__ out) {
   griddep_wait();
@@ -681,8 +687,10 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
         o[c] += __uint_as_float((uint32_t)wv);
       }
     }
-    *reinterpret_cast<float4*>(out + (int64_t)(t0 + tl) * H + 4 * h4) =
-        make_float4(o[0], o[1], o[2], o[3]);
+    const int64_t i = (int64_t)(t0 + tl) * H + 4 * h4;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[c] = residual_out(res, i + c, o[c]);
+    *reinterpret_cast<float4*>(out + i) = make_float4(o[0], o[1], o[2], o[3]);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1621,7 +1629,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
       ce = launch_pdl(k_combine_ar, dim3(blocks), dim3(256), 0, stream,
                       reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
                       (const int4*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
-                      g.jmaxB, t0, Tc, *comm,
+                      g.jmaxB, t0, Tc, *comm, p.res,
                       reinterpret_cast<uint32_t*>(ws), out);
       if (ce != cudaSuccess) return cuda_fail(ce, "combine (all-reduce) launch");
     }
@@ -1630,7 +1638,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
                   (const int4*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
-                  reinterpret_cast<float4*>(out));
+                  p.res, reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 

@@ -37,6 +37,15 @@ constexpr uint64_t kPeerWaitDefaultNs = 2000000000ull;
 // The kernel's view of an open communicator on the current device.
 wr_status_t comm_view(const wr_comm* c, CommView* v);
 
+// The residual connection of a decode stack, fused into a layer's last
+// step: out = x + layer(x) (fp32), and next_x = out rounded to the layer's
+// dtype (the next layer's input).  x == null: no residual.
+struct Residual {
+  const void* x;   // [T, H] in the layer dtype
+  void* next_x;    // [T, H] in the layer dtype, or null
+  int bf16;        // layer dtype is bf16 (else fp32)
+};
+
 // Per-call problem description after validation.
 struct Problem {
   int E, H, I, K, T;          // experts, hidden, intermediate, top_k, tokens
@@ -44,6 +53,7 @@ struct Problem {
   int dtype;                  // wr_dtype_t
   int elt;                    // bytes per element
   const float* router_bias;   // optional [E]
+  Residual res;               // res.x == null: no fused residual
 };
 
 // Sets the thread's last-error text (printf-style) and returns `s`.

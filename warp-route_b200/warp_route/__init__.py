@@ -18,6 +18,7 @@ from .functional import (
     fused_moe,
     fused_moe_batched,
     fused_moe_routed,
+    moe_decode_layer,
     naive_moe,
     pack_expert_shard,
     router_topk,
@@ -30,6 +31,7 @@ __all__ = [
     "batched_fused_moe",
     "fused_moe_batched",
     "fused_moe_routed",
+    "moe_decode_layer",
     "router_topk",
     "pack_expert_shard",
     "_pack_expert_weights",

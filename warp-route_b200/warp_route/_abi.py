@@ -79,6 +79,8 @@ SIGNATURES = {
     "wr_comm_reset": (_i32, [_vp, _vp]),
     "wr_fused_moe_allreduce": (_i32, [_D, _i32, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp,
                                       _vp]),
+    "wr_moe_decode_layer": (_i32, [_D, _i32, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz,
+                                   _vp, _vp]),
 }
 
 _lib = None

@@ -5,14 +5,19 @@ each (src/bindings.cpp:55,94,140); its README motivates the kernels with
 decode-step latency (README.md:17).  `MoEStack` captures the whole stack of
 layer calls for a fixed token count once and replays it every step:
 
-    h_0 = x;   h_{l+1} = h_l + moe_l(h_l)   (residual add, in the layer dtype)
+    h_0 = x;   h_{l+1} = (h_l + moe_l(h_l)).to(dtype)   (residual, fp32 add, one rounding)
 
-Each moe_l is this package's fused layer (`fused_moe_routed`: the streaming
-kernel for one token, the grouped tcgen05 path for a batch), optionally
-followed by a sum over ranks (`all_reduce`, e.g. torch.distributed.all_reduce
-on an NCCL group: it is captured into the same graph) for tensor- or
-expert-parallel shards.  Inputs and outputs live in static device buffers;
-`step(x)` copies x in, replays, and returns the output buffer.
+Each layer is ONE kernel launch chain of this package: `moe_decode_layer`
+writes both the fp32 sum and the next layer's input from the layer's last
+step (the streaming kernel for a token, the grouped tcgen05 path for a
+batch), so consecutive layers follow each other with programmatic dependent
+launch and no element-wise kernels in between.  Tensor- or expert-parallel
+shards pass `comm` (a `PeerComm`): the ranks' partial outputs are summed in
+the same kernel before the residual.  An external collective (`all_reduce`,
+e.g. torch.distributed.all_reduce on NCCL, captured into the same graph)
+still works; the residual is then added after it, as two extra kernels.
+Inputs and outputs live in static device buffers; `step(x)` copies x in,
+replays, and returns the output buffer.
 """
 from __future__ import annotations
 
@@ -21,7 +26,7 @@ from typing import Callable, List, Optional
 
 import torch
 
-from .functional import fused_moe_routed
+from .functional import PeerComm, fused_moe_routed, moe_decode_layer
 
 
 @dataclass
@@ -38,13 +43,17 @@ class StackLayer:
 class MoEStack:
     def __init__(self, layers: List[StackLayer], num_experts: int, hidden_dim: int,
                  intermediate_dim: int, top_k: int, tokens: int,
-                 all_reduce: Optional[Callable[[torch.Tensor], None]] = None):
+                 all_reduce: Optional[Callable[[torch.Tensor], None]] = None,
+                 comm: Optional[PeerComm] = None):
         if not layers:
             raise ValueError("MoEStack needs at least one layer")
+        if all_reduce is not None and comm is not None:
+            raise ValueError("pass either comm (fused sum) or all_reduce (external), not both")
         self.layers = layers
         self.E, self.H, self.I, self.K = num_experts, hidden_dim, intermediate_dim, top_k
         self.T = tokens
         self.all_reduce = all_reduce
+        self.comm = comm
         dev = layers[0].gate_w.device
         self.dtype = layers[0].gate_w.dtype
         shape = (hidden_dim,) if tokens == 1 else (tokens, hidden_dim)
@@ -53,22 +62,29 @@ class MoEStack:
         self.stream = torch.cuda.Stream(device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
-    def _layer(self, L: StackLayer, h: torch.Tensor) -> torch.Tensor:
+    def layer(self, i: int, h: torch.Tensor, nxt: torch.Tensor) -> torch.Tensor:
+        """Layer i on input h: writes the next input into nxt and returns the
+        layer's fp32 output (residual included)."""
+        L = self.layers[i]
+        if self.all_reduce is None:
+            return moe_decode_layer(h, L.gate_w, L.weight_buf, self.E, self.H, self.I, self.K,
+                                    next_x=nxt, comm=self.comm, router_bias=L.router_bias,
+                                    ep_first_expert=L.ep_first_expert,
+                                    ep_num_local=L.ep_num_local)
         out, _, _ = fused_moe_routed(h, L.gate_w, L.weight_buf, self.E, self.H, self.I, self.K,
                                      router_bias=L.router_bias,
                                      ep_first_expert=L.ep_first_expert,
                                      ep_num_local=L.ep_num_local)
-        if self.all_reduce is not None:
-            self.all_reduce(out)
+        self.all_reduce(out)
+        torch.add(h.float(), out, out=out)
+        nxt.copy_(out)
         return out
 
     def _forward(self) -> torch.Tensor:
         h = self.x_in
-        for i, L in enumerate(self.layers):
-            out = self._layer(L, h)
+        for i in range(len(self.layers)):
             nxt = self.h[i & 1]
-            torch.add(h.float(), out, out=out)
-            nxt.copy_(out)
+            self.layer(i, h, nxt)
             h = nxt
         return h
 
@@ -80,6 +96,9 @@ class MoEStack:
     def capture(self, warmup: int = 2) -> None:
         """Capture the stack into a CUDA graph (warm-up calls run first, on the
         capture stream, so the per-stream workspaces exist before capture)."""
+        # the capture stream's warm-up writes the same static buffers as any
+        # call already queued on the caller's stream: run it after them
+        self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             for _ in range(warmup):
                 self._forward()

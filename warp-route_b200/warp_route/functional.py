@@ -307,6 +307,34 @@ class PeerComm:
             self._ptr = 0
 
 
+def moe_decode_layer(
+    x: torch.Tensor,
+    gate_w: torch.Tensor,
+    weight_buf: torch.Tensor,
+    num_experts: int,
+    hidden_dim: int,
+    intermediate_dim: int,
+    top_k: int,
+    *,
+    next_x: Optional[torch.Tensor] = None,
+    comm: Optional["PeerComm"] = None,
+    router_bias: Optional[torch.Tensor] = None,
+    ep_first_expert: int = 0,
+    ep_num_local: int = 0,
+) -> torch.Tensor:
+    """One layer of a decode stack with the residual connection fused into
+    the layer kernel's last step: returns out = x + layer(x) (float32; with
+    `comm`, the layer is this rank's shard and the sum over the ranks comes
+    first) and, if `next_x` is given (x's shape and dtype, not x itself),
+    writes next_x = out.to(x.dtype) — the next layer's input — from the same
+    kernel.  Bit-identical to `(x.float() + layer(x)).to(x.dtype)`, with no
+    extra kernels per layer."""
+    _C = _load_extension()
+    return _C.moe_decode_layer(x, gate_w, weight_buf, num_experts, hidden_dim,
+                               intermediate_dim, top_k, comm.handle if comm is not None else 0,
+                               router_bias, ep_first_expert, ep_num_local, next_x)
+
+
 def fused_moe_allreduce(
     x: torch.Tensor,
     gate_w: torch.Tensor,
