@@ -241,15 +241,24 @@ WR_DEVINL void dot_pair_bf16(const uint4* __restrict__ gp, const uint4* __restri
   }
 }
 
-// Phase B dot of one down-row piece over chunks j0, j0 + js, ... < nch
-// against the activation window (layout [column][NT]).
-template <typename Tw, int NT>
-WR_DEVINL void dot_down(const uint4* __restrict__ wp, const float* __restrict__ av, int nch,
-                        int j0, int js, float (&acc)[NT]) {
+// Phase B dot products of nr <= R rows of one stage (row r's chunks start at
+// wp + r * rs) over chunks j0, j0 + js, ... < nch against the activation
+// window (layout [column][NT]): acc[r][t] += row r . act[:, t].  Each
+// activation chunk is loaded from shared memory once for all the rows (one
+// row at a time would read the fp32 window once per row: twice the bytes of
+// the bf16 weights).  Per row, products alternate between two accumulators
+// by chunk half (acc: even 4-element groups, acc1: odd), added at the end.
+template <typename Tw, int NT, int R>
+WR_DEVINL void dot_down_rows(const uint4* __restrict__ wp, int rs, const float* __restrict__ av,
+                             int nch, int j0, int js, int nr, float (&acc)[R][NT]) {
   constexpr int VEC = Chunk<Tw>::kVec;
-  float acc1[NT];
+  constexpr int UF = R == 1 ? 4 : 2;  // loop unroll: loads of UF chunks in flight
+  float acc1[R][NT];
 #pragma unroll
-  for (int t = 0; t < NT; ++t) acc1[t] = 0.0f;
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc1[r][t] = 0.0f;
+  }
   if constexpr (VEC == 8 && NT == 1) {
     // bf16, one token: a lane's 8 activations are 32 bytes, so lanes 4 apart
     // would hit the same shared-memory banks.  Lanes with bit 2 set read the
@@ -257,44 +266,61 @@ WR_DEVINL void dot_down(const uint4* __restrict__ wp, const float* __restrict__ 
     // order): each group of 8 lanes then covers 8 distinct bank slots.  Those
     // lanes fill acc and acc1 in swapped roles, and acc + acc1 is the same.
     const int hs = (j0 & 4) ? 4 : 0;
-#pragma unroll 4
+#pragma unroll UF
     for (int j = j0; j < nch; j += js) {
-      const uint4 w = wp[j];
       const float4 aA = *reinterpret_cast<const float4*>(av + j * 8 + hs);
       const float4 aB = *reinterpret_cast<const float4*>(av + j * 8 + (4 - hs));
-      const uint32_t wA0 = hs ? w.z : w.x, wA1 = hs ? w.w : w.y;
-      const uint32_t wB0 = hs ? w.x : w.z, wB1 = hs ? w.y : w.w;
-      acc[0] = fmaf(bf16lo(wA0), aA.x, acc[0]);
-      acc[0] = fmaf(bf16hi(wA0), aA.y, acc[0]);
-      acc[0] = fmaf(bf16lo(wA1), aA.z, acc[0]);
-      acc[0] = fmaf(bf16hi(wA1), aA.w, acc[0]);
-      acc1[0] = fmaf(bf16lo(wB0), aB.x, acc1[0]);
-      acc1[0] = fmaf(bf16hi(wB0), aB.y, acc1[0]);
-      acc1[0] = fmaf(bf16lo(wB1), aB.z, acc1[0]);
-      acc1[0] = fmaf(bf16hi(wB1), aB.w, acc1[0]);
-    }
-    acc[0] += acc1[0];
-    return;
-  }
-#pragma unroll 4
-  for (int j = j0; j < nch; j += js) {
-    float wf[VEC];
-    Chunk<Tw>::widen(wp[j], wf);
-    const float4* a4p = reinterpret_cast<const float4*>(av + j * VEC * NT);
 #pragma unroll
-    for (int q4 = 0; q4 < VEC * NT / 4; ++q4) {
-      const float4 a4 = a4p[q4];
-      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
-#pragma unroll
-      for (int z = 0; z < 4; ++z) {
-        const int flat = 4 * q4 + z;  // = q * NT + t
-        float& ac = ((flat / NT) & 1) ? acc1[flat % NT] : acc[flat % NT];
-        ac = fmaf(wf[flat / NT], av4[z], ac);
+      for (int r = 0; r < R; ++r) {
+        if (r < nr) {
+          const uint4 w = wp[r * rs + j];
+          const uint32_t wA0 = hs ? w.z : w.x, wA1 = hs ? w.w : w.y;
+          const uint32_t wB0 = hs ? w.x : w.z, wB1 = hs ? w.y : w.w;
+          acc[r][0] = fmaf(bf16lo(wA0), aA.x, acc[r][0]);
+          acc[r][0] = fmaf(bf16hi(wA0), aA.y, acc[r][0]);
+          acc[r][0] = fmaf(bf16lo(wA1), aA.z, acc[r][0]);
+          acc[r][0] = fmaf(bf16hi(wA1), aA.w, acc[r][0]);
+          acc1[r][0] = fmaf(bf16lo(wB0), aB.x, acc1[r][0]);
+          acc1[r][0] = fmaf(bf16hi(wB0), aB.y, acc1[r][0]);
+          acc1[r][0] = fmaf(bf16lo(wB1), aB.z, acc1[r][0]);
+          acc1[r][0] = fmaf(bf16hi(wB1), aB.w, acc1[r][0]);
+        }
       }
     }
-  }
 #pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t] += acc1[t];
+    for (int r = 0; r < R; ++r) acc[r][0] += acc1[r][0];
+  } else {
+#pragma unroll UF
+    for (int j = j0; j < nch; j += js) {
+      float af[VEC * NT];
+      const float4* a4p = reinterpret_cast<const float4*>(av + j * VEC * NT);
+#pragma unroll
+      for (int q4 = 0; q4 < VEC * NT / 4; ++q4) {
+        const float4 a4 = a4p[q4];
+        af[4 * q4 + 0] = a4.x;
+        af[4 * q4 + 1] = a4.y;
+        af[4 * q4 + 2] = a4.z;
+        af[4 * q4 + 3] = a4.w;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (r < nr) {
+          float wf[VEC];
+          Chunk<Tw>::widen(wp[r * rs + j], wf);
+#pragma unroll
+          for (int flat = 0; flat < VEC * NT; ++flat) {  // flat = q * NT + t
+            float& ac = ((flat / NT) & 1) ? acc1[r][flat % NT] : acc[r][flat % NT];
+            ac = fmaf(wf[flat / NT], af[flat], ac);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[r][t] += acc1[r][t];
+    }
+  }
 }
 
 template <int NT>
@@ -891,16 +917,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     if (!ok && lane == 0) *abort_flag = 1;
     for (int i = tid; i < W * pl.NBM * NT; i += kConsumerThreads) rowacc[i] = 0.0f;
 
-    // ---- phase B: down rows, slot by slot.  Each row is read by PB warps,
-    // each taking a column slice; warp w adds into its own accumulators
-    // rowacc[w][h][t], summed in warp order at the end.  The activation
-    // window of (slot s, window win) is the j-th, in buffer j % CB; the
-    // publisher warp fills it, and each warp releases it after its rows. ----
+    // ---- phase B: down rows, slot by slot.  Local row lr of a stage is read
+    // by the PB warps of row group lr % GW, each taking a column slice; a
+    // warp computes its (up to kRowsPerWarp) rows of the stage together, so
+    // they share every activation load.  Warp w adds into its own
+    // accumulators rowacc[w][h][t], summed in warp order at the end.  The
+    // activation window of (slot s, window win) is the j-th, in buffer j % CB;
+    // the publisher warp fills it, and each warp releases it after its rows
+    // of the window. ----
     {
       const int GW = W / pl.PB;         // row groups of PB warps
       const int partB = warp % pl.PB;   // my column slice
       const int grpB = warp / pl.PB;    // my row group
       named_bar_sync(kBarConsumers, kConsumerThreads);  // row accumulators zeroed
+      const int rs = pl.WB / VEC;  // 16-byte chunks from one stage row to the next
       int j = 0;
       for (int s = 0; s < S; ++s) {
         for (int win = 0; win < pl.nwin; ++win, ++j) {
@@ -918,30 +948,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
             // `part` of them taking chunks part*32 + lane + PB*32*k
             const int lr0 = hb - hb0;  // local row of the stage's first row
             const int first = (grpB - (lr0 & (GW - 1)) + GW) & (GW - 1);  // my first row of it
-            float* racc = rowacc + ((int64_t)warp * pl.NBM + lr0) * NT;
-            if (ok && first < g) ok = wait_owned();
-            if (ok && first < g) {
-              const uint8_t* st = ring + c.si * pl.SB;
+            const int nr = first < g ? (g - first + GW - 1) / GW : 0;    // my rows: first + k GW
+            float* racc = rowacc + ((int64_t)warp * pl.NBM + lr0 + first) * NT;
+            if (ok && nr > 0) ok = wait_owned();
+            if (ok && nr > 0) {
+              const uint4* wp = reinterpret_cast<const uint4*>(ring + c.si * pl.SB) + first * rs;
+              const int j0 = partB * 32 + lane, js = pl.PB * 32;
               float v[kRowsPerWarp][NT];
 #pragma unroll
-              for (int k = 0; k < kRowsPerWarp; ++k) {
+              for (int r = 0; r < kRowsPerWarp; ++r) {
 #pragma unroll
-                for (int t = 0; t < NT; ++t) v[k][t] = 0.0f;
-                const int rr = first + k * GW;
-                if (rr < g)
-                  dot_down<Tw, NT>(reinterpret_cast<const uint4*>(st + rr * pl.WB * ELT), av, nch,
-                                   partB * 32 + lane, pl.PB * 32, v[k]);
+                for (int t = 0; t < NT; ++t) v[r][t] = 0.0f;
+              }
+              if (nr == 1) {  // one row: the deeper-unrolled loop
+                float v1[1][NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) v1[0][t] = 0.0f;
+                dot_down_rows<Tw, NT, 1>(wp, GW * rs, av, nch, j0, js, 1, v1);
+#pragma unroll
+                for (int t = 0; t < NT; ++t) v[0][t] = v1[0][t];
+              } else if (nr == 2) {
+                float v2[2][NT];
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+#pragma unroll
+                  for (int t = 0; t < NT; ++t) v2[r][t] = 0.0f;
+                }
+                dot_down_rows<Tw, NT, 2>(wp, GW * rs, av, nch, j0, js, 2, v2);
+#pragma unroll
+                for (int r = 0; r < 2; ++r) {
+#pragma unroll
+                  for (int t = 0; t < NT; ++t) v[r][t] = v2[r][t];
+                }
+              } else {
+                dot_down_rows<Tw, NT, kRowsPerWarp>(wp, GW * rs, av, nch, j0, js, nr, v);
               }
               __syncwarp();
               if (lane == 0) mbar_arrive(&empty[c.si]);
 #pragma unroll
-              for (int k = 0; k < kRowsPerWarp; ++k) {
-                const int rr = first + k * GW;
-                if (rr < g) {
-                  warp_sum<NT>(v[k]);
+              for (int r = 0; r < kRowsPerWarp; ++r) {
+                if (r < nr) {
+                  warp_sum<NT>(v[r]);
                   if (lane == 0) {
 #pragma unroll
-                    for (int t = 0; t < NT; ++t) racc[rr * NT + t] += v[k][t];
+                    for (int t = 0; t < NT; ++t) racc[r * GW * NT + t] += v[r][t];
                   }
                 }
               }
@@ -1005,15 +1055,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   }
   if (tid == 0) {
     // Self-reset of the slot counters: every CTA has left its waits once it
-    // counts itself out, so the last one can clear them all.
+    // counts itself out, so the last one can clear them all.  The fence makes
+    // this CTA's counter increments (made by other warps, ordered before by
+    // the barrier) visible before its exit count; the clears are plain
+    // stores, visible to the next launch once this one has completed.
     __threadfence();
     const uint32_t prev = atomicAdd(&a.sync[kSyncExit], 1u);
     if (prev == (uint32_t)G - 1) {
-      for (int s = 0; s < S; ++s) atomicExch(&a.sync[kSyncSlot0 + s], 0u);
-      atomicExch(&a.sync[kSyncRouter], 0u);
+      for (int s = 0; s < S; ++s) a.sync[kSyncSlot0 + s] = 0u;
+      a.sync[kSyncRouter] = 0u;
       if (a.comm.world > 0) *a.comm.epoch = *s_epoch;  // the next launch uses epoch + 1
-      atomicExch(&a.sync[kSyncExit], 0u);
-      __threadfence();
+      a.sync[kSyncExit] = 0u;
     }
   }
 }
