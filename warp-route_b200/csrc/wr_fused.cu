@@ -96,7 +96,10 @@ constexpr int kMaxActBufs = 16;    // phase B: activation window buffers, at mos
 constexpr int kOffActBars = 5376;  // mbarrier act_full[16], act_empty[16]
 static_assert(kOffBars + 8 * (2 * kMaxStages) <= kOffAbort, "misc");
 static_assert(kOffLogits + 4 * kMaxNT * kMaxExperts <= kOffActBars, "misc");
-static_assert(kOffActBars + 16 * kMaxActBufs <= kMiscBytes, "misc");
+constexpr int kOffLParts = 5632;   // float [T][segment][E]: a small router's partial sums
+constexpr int kLPartsBytes = 512;  // (<= 2 items per consumer warp: T * E <= 16)
+static_assert(kOffActBars + 16 * kMaxActBufs <= kOffLParts, "misc");
+static_assert(kOffLParts + kLPartsBytes <= kMiscBytes, "misc");
 static_assert(kOffTokW + 4 * kMaxNT * kMaxExperts <= kOffSlotBar, "misc");
 static_assert(kOffSlotBar + 8 * kMaxExperts <= kOffLogits, "misc");
 static_assert(kOffLogits + 4 * kMaxNT * kMaxExperts <= kMiscBytes, "misc");
@@ -513,11 +516,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   // partial sums: item (token t, row batch eb, segment seg) is segment seg of
   // router rows [8 eb, 8 eb + 8) against x_t (the fixed order of
   // wr_router.cuh).  Small routers (pl.localR) are computed whole by every
-  // CTA into shared memory (the ring is idle until the selection); larger
-  // ones are spread over every consumer warp of the grid and meet in the
-  // workspace behind one grid-wide counter.
+  // CTA into a small shared-memory area; larger ones are spread over every
+  // consumer warp of the grid and meet in the workspace behind one grid-wide
+  // counter.
   const int nbat = (E + kRouterRowBatch - 1) / kRouterRowBatch;
-  float* lparts = reinterpret_cast<float*>(ring);  // [T][segment][E] when pl.localR
+  float* lparts = reinterpret_cast<float*>(misc + kOffLParts);  // [T][segment][E] when pl.localR
   if (warp >= W && kBf16) {
     // bf16 x kept as is: [NT][H] chunks (tokens >= T are zero)
     const uint4* xg = static_cast<const uint4*>(a.x);
@@ -644,8 +647,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   } else if (warp == W) {
     // =========================== producer ===================================
     if (lane == 0) {
-      // the ring held router partial sums (generic writes) until the selection
-      fence_proxy_async_smem();
+      // (nothing but the bulk copies writes the ring, so no proxy fence is
+      // needed before the first one)
       const uint64_t pol = l2_policy_evict_first();
       bool ok = true;
       int issued = 0;
@@ -1203,12 +1206,13 @@ Plan make_plan(const Problem& p, int nt, int grid) {
     pl.nst = (int)nst_ov;
   }
   // Every CTA computes the whole router when it is small (<= 2 items per
-  // consumer warp, <= 64 KB of router weights read from L2 by each CTA, the
-  // partial sums fit in the ring); otherwise the items are spread over the grid.
+  // consumer warp, <= 64 KB of router weights read from L2 by each CTA; the
+  // partial sums then fit in kLPartsBytes of shared memory); otherwise the
+  // items are spread over the grid.
   const int64_t items =
       (int64_t)nt * ((p.E + kRouterRowBatch - 1) / kRouterRowBatch) * kRouterSegments;
   pl.localR = (items <= 2 * kConsumerWarps && (int64_t)p.E * p.H * elt <= 64 * 1024 &&
-               (int64_t)nt * kRouterSegments * p.E * 4 <= (int64_t)pl.nst * pl.SB)
+               (int64_t)nt * kRouterSegments * p.E * 4 <= kLPartsBytes)
                   ? 1
                   : 0;
   return pl;
