@@ -114,11 +114,24 @@ WR_DEVINL float router_combine(const float* parts, int stride, int e, const floa
   return l;
 }
 
+// Order-preserving key of a logit for the top-K rounds: a larger float gives
+// a larger unsigned key; NaN ranks as -inf and -0 as +0 (so the keys compare
+// exactly as the floats do under '>').  Key 0 is below every logit.
+WR_DEVINL uint32_t logit_key(float v) {
+  if (v != v) v = __int_as_float(0xff800000);
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // Softmax + top-K for one token, run by one full warp.
-// logits [E] (E <= 64, any memory) -> ids [K], weights [K] (written by lane 0).
+// logits [E] (E <= 64, any memory) -> ids [K], weights [K] (written by lanes
+// 0..K-1).
 // Selection: K rounds of "largest key, lowest index on ties" over the unused
 // experts, key = logit (NaN counts as -inf) — warp-route's strict-'>'
-// argmax (src/fused_moe.cu:134-142) with ties to the lowest index.
+// argmax (src/fused_moe.cu:134-142) with ties to the lowest index.  A round
+// is one warp max-reduction of the keys (lane l holds experts l and l + 32)
+// and two ballots for the lowest index holding the maximum.
 // Softmax: m = max logit; p_e = exp(l_e - m); the sum is a fixed tree —
 // lane l adds p_l + p_{l+32}, then a 16/8/4/2/1 xor tree; weight_k =
 // p_{id_k} / sum.
@@ -136,30 +149,22 @@ WR_DEVINL void select_topk_warp(const float* logits, int E, int K, int lane, int
   float s = __fadd_rn(p0, p1);
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-  bool used0 = e0 >= E, used1 = e1 >= E;
+  uint32_t k0 = e0 < E ? logit_key(l0) : 0u;  // 0: absent or already selected
+  uint32_t k1 = e1 < E ? logit_key(l1) : 0u;
+  int mine = -1;  // lane k keeps the k-th selected expert
   for (int k = 0; k < K; ++k) {
-    // this lane's best unused candidate
-    float kv = ninf;
-    int ki = 1 << 20;
-    if (!used0) { kv = (l0 != l0) ? ninf : l0; ki = e0; }
-    if (!used1) {
-      const float v1 = (l1 != l1) ? ninf : l1;
-      if (ki == (1 << 20) || v1 > kv) { kv = v1; ki = e1; }
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, kv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, ki, off);
-      if (ov > kv || (ov == kv && oi < ki)) { kv = ov; ki = oi; }
-    }
-    if (ki == e0) used0 = true;
-    if (ki == e1) used1 = true;
-    // the lane holding expert ki (lane ki & 31) supplies its probability
-    const float pb = __shfl_sync(0xffffffffu, (ki == e0) ? p0 : p1, ki & 31);
-    if (lane == 0) {
-      ids[k] = ki;
-      weights[k] = __fdiv_rn(pb, s);
-    }
+    const uint32_t best = __reduce_max_sync(0xffffffffu, k0 > k1 ? k0 : k1);
+    const unsigned b0 = __ballot_sync(0xffffffffu, k0 == best);
+    const unsigned b1 = __ballot_sync(0xffffffffu, k1 == best);
+    const int ki = b0 ? __ffs(b0) - 1 : 32 + __ffs(b1) - 1;  // experts l < experts l + 32
+    if (ki == e0) k0 = 0u;
+    if (ki == e1) k1 = 0u;
+    if (lane == k) mine = ki;
+  }
+  if (lane < K) {
+    const float pe = expf(logits[mine] - m);  // the same value as p0 / p1 of its lane
+    ids[lane] = mine;
+    weights[lane] = __fdiv_rn(pe, s);
   }
 }
 
