@@ -70,6 +70,8 @@ constexpr int kThreads = kConsumerThreads + 64;  // + producer warp + publisher 
 constexpr int kTargetStage = 32 * 1024;          // stage size aimed for
 constexpr int kMaxStageBytes = 32 * 1024;
 constexpr int kMaxStages = 12;
+constexpr int kWideStageBytes = 48 * 1024;   // two-row-pair stages (make_plan_v)
+constexpr int kWideWindowBytes = 24 * 1024;  // their activation windows, at most
 constexpr int kSmemBytes = 232448;  // 227 KB: the sm_100 per-CTA opt-in maximum
 constexpr int kMiscBytes = 8192;
 constexpr int kMiscOff = kSmemBytes - kMiscBytes;
@@ -1129,14 +1131,22 @@ int clamp_rows(int64_t g) {
   return (int)(g > kMaxRowsPerStage ? kMaxRowsPerStage : g);
 }
 
-Plan make_plan(const Problem& p, int nt, int grid) {
+// wide: stages of two whole row pairs of more than 16 KB (copies of 2 rows,
+// 32-48 KB stages: a one-row-pair stage would issue copies of one row of
+// 8-16 KB, which stream from HBM more slowly), with activation windows of at
+// most 24 KB so that the ring still holds 4 stages.
+Plan make_plan_v(const Problem& p, int nt, int grid, bool wide) {
   const int elt = p.elt, vec = 16 / elt;
   Plan pl;
   // phase A: whole row pairs when one fits in a stage, else pieces of
   // kTargetStage / 2 bytes of one gate row and one up row
   const int64_t pair = 2LL * p.H * elt;
   int stage_a;
-  if (pair <= kMaxStageBytes) {
+  if (wide) {
+    pl.GA = 2;
+    pl.CWA = p.H;
+    stage_a = (int)(2 * pair);
+  } else if (pair <= kMaxStageBytes) {
     pl.GA = clamp_rows(kTargetStage / pair);
     pl.CWA = p.H;
     stage_a = (int)(pl.GA * pair);
@@ -1148,6 +1158,7 @@ Plan make_plan(const Problem& p, int nt, int grid) {
   // phase B: windows of at most kTargetStage bytes of weight columns
   int64_t wmax = (int64_t)kVecMaxBytes / (nt * 4);
   if (wmax > kTargetStage / elt) wmax = kTargetStage / elt;
+  if (wide && wmax > kWideWindowBytes / (nt * 4)) wmax = kWideWindowBytes / (nt * 4);
   wmax = wmax / vec * vec;
   if (p.I <= wmax) {
     pl.nwin = 1;
@@ -1215,6 +1226,16 @@ Plan make_plan(const Problem& p, int nt, int grid) {
                (int64_t)nt * kRouterSegments * p.E * 4 <= kLPartsBytes)
                   ? 1
                   : 0;
+  return pl;
+}
+
+Plan make_plan(const Problem& p, int nt, int grid) {
+  const Plan pl = make_plan_v(p, nt, grid, false);
+  const int64_t pair = 2LL * p.H * p.elt;
+  if (pl.GA == 1 && pl.CWA == p.H && pair > kTargetStage / 2 && 2 * pair <= kWideStageBytes) {
+    const Plan w = make_plan_v(p, nt, grid, true);
+    if (w.nst >= 4) return w;
+  }
   return pl;
 }
 
