@@ -1168,10 +1168,18 @@ Plan make_plan_v(const Problem& p, int nt, int grid, bool wide) {
     int64_t w = (p.I + pl.nwin - 1) / pl.nwin;
     pl.WB = (int)((w + vec - 1) / vec * vec);
   }
+  // phase B: the CTA's rows of a window in as few stages of at most
+  // kWideStageBytes as they fit, split evenly (the consumers pay a fixed cost
+  // per stage, and a short last stage costs as much as a full one)
   const int64_t row_b = (int64_t)pl.WB * elt;
-  int sb = stage_a > (int)row_b ? stage_a : (int)row_b;
+  const int64_t nbm = (p.H + grid - 1) / grid;
+  int64_t gb_max = kWideStageBytes / row_b;
+  if (gb_max > kMaxRowsPerStage) gb_max = kMaxRowsPerStage;
+  if (gb_max < 1) gb_max = 1;
+  const int64_t nstg = (nbm + gb_max - 1) / gb_max;
+  pl.GB = clamp_rows((nbm + nstg - 1) / nstg);
+  int sb = stage_a > (int)(pl.GB * row_b) ? stage_a : (int)(pl.GB * row_b);
   sb = (sb + 127) / 128 * 128;
-  pl.GB = clamp_rows(sb / row_b);
   pl.SB = sb;
   // Long rows are split by columns over PB warps (shorter holds of each
   // stage); a warp then reads at most kRowsPerWarp rows of a stage.
