@@ -110,6 +110,33 @@ def test_hot_expert_spans_several_token_tiles():
     _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, 128, 129, 299], bias)
 
 
+@pytest.mark.parametrize("E,H,I,T,rows", [
+    # few K chunks: nearly every gate/up tile is cut between CTAs (partial
+    # sums parked and added by the tile's last CTA); every token checked
+    (4, 1024, 1536, 250, None),
+    # more tiles than CTAs: whole tiles run in one CTA
+    (8, 1024, 4096, 250, [0, 5, 127, 128, 129, 200, 249]),
+    # 129 tokens: the second accumulator holds one token
+    (4, 1024, 1536, 129, None),
+])
+def test_gate_up_tiles_above_128_tokens(E, H, I, T, rows):
+    """Batches above 128 tokens: an expert's gate/up tile of up to 256 tokens
+    streams its weights once, tokens 128.. from a second token slot into the
+    second TMEM accumulator.  A bias sends every token to expert 2 first."""
+    K = 2
+    L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=23, tokens=T)
+    bias = torch.zeros(E, dtype=torch.float32, device="cuda")
+    bias[2] = 50.0
+    out, ids, w = abi_layer(L.x, L.gate_w, L.weight_buf, E, H, I, K, bias=bias)
+    torch.cuda.synchronize()
+    assert (ids[:, 0] == 2).all()
+    o_ids, o_w = _router_ids(L.x, L.gate_w, K, bias)
+    np.testing.assert_array_equal(ids.cpu().numpy(), o_ids)
+    np.testing.assert_allclose(w.cpu().numpy(), o_w, rtol=2e-6, atol=1e-7)
+    _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K,
+                list(range(T)) if rows is None else rows, bias)
+
+
 @pytest.mark.parametrize("E,H,I,K,T", [
     (8, 1000, 1000, 2, 20),    # row tiles and K chunks with tails (TMA zero fill)
     (4, 64, 64, 2, 8),         # one K chunk, one row tile smaller than the MMA

@@ -64,7 +64,8 @@ constexpr int kTokM = 128;               // MMA M: token rows (the tile's n, res
 constexpr int kWRows = 256;              // MMA N: weight rows per MMA
 constexpr int kRowsA = 128;              // gate/up tile: rows of gate and of up
 constexpr int kRowsB = 256;              // down tile: rows of Wd (= rows of H)
-constexpr int kNMaxA = kTokM;            // tokens per gate/up tile
+constexpr int kNMaxA = kTokM;            // tokens per gate/up tile (one accumulator)
+constexpr int kNMaxAWide = 2 * kTokM;    // ... above 128 tokens: both accumulators (T > 128)
 constexpr int kNMaxB = 64;               // tokens per down accumulator (act_hi, act_lo: 128 A rows)
 constexpr int kNMaxBWide = 128;          // tokens per down tile above 64 tokens: both accumulators
 constexpr int kRowB = kBK * 2;           // bytes of one row per stage
@@ -90,11 +91,13 @@ constexpr int kJMaxBLimit = 16;          // ... and at most this one (few tiles:
 
 // Bucket metadata (int32 words in the workspace), written by the bucketing:
 //   [0] rows in use, [1] gate/up tiles, [2] down tiles, [3] down cost, [4]
-//   the largest down chunk cost present, and from word 16 cnt[E], base[E], ntlA[E], ntlB[E] (token tiles per expert),
-//   preA[E+1], preB[E+1] (tiles before each expert), costB[E+1] (down cost
-//   before each expert, see down_chunk_cost).
+//   the largest down chunk cost present, [5] gate/up cost, [6] the largest
+//   gate/up chunk cost present, and from word 16 cnt[E], base[E], ntlA[E],
+//   ntlB[E] (token tiles per expert), preA[E+1], preB[E+1] (tiles before
+//   each expert), costB[E+1], costA[E+1] (down / gate/up cost before each
+//   expert, see chunk_cost).
 constexpr int kMetaHdr = 16;
-__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 7 * E + 3; }
+__host__ __device__ inline int meta_words(int E) { return kMetaHdr + 8 * E + 4; }
 struct MetaView {
   const int* cnt;
   const int* base;
@@ -103,6 +106,7 @@ struct MetaView {
   const int* preA;
   const int* preB;
   const int* costB;
+  const int* costA;
 };
 __host__ __device__ inline MetaView meta_view(const int* m, int E) {
   MetaView v;
@@ -113,30 +117,38 @@ __host__ __device__ inline MetaView meta_view(const int* m, int E) {
   v.preA = v.ntlB + E;
   v.preB = v.preA + E + 1;
   v.costB = v.preB + E + 1;
+  v.costA = v.costB + E + 1;
   return v;
 }
 
-// Down work is split by cost, not by chunk count.  With tiles above 64
-// tokens (both accumulators, two MMAs per K step) a chunk costs 6 units
-// there and 5 elsewhere (measured: such CTAs ran about 1.2x as long per
-// chunk); otherwise every chunk costs 1, which is the plain chunk split.
+// Work is split by cost, not by chunk count.  When a launch has wide tiles
+// (gate/up: above 128 tokens, two MMAs and two token slots per K step;
+// down: above 64 tokens, two MMAs per K step) a chunk of a wide tile costs
+// kCostWideA / kCostWideB units and any other chunk kCostOne (measured: the
+// CTAs holding wide down chunks ran about 1.2x as long per chunk, wide
+// gate/up chunks about 1.4x); otherwise every chunk costs 1, which is the
+// plain chunk split.
 constexpr int kCostOne = 5;
-constexpr int kCostWide = 6;
-__host__ __device__ inline int down_chunk_cost(int n, int nmaxB) {
-  return nmaxB > kNMaxB ? (n > kNMaxB ? kCostWide : kCostOne) : 1;
+constexpr int kCostWideA = 7;
+constexpr int kCostWideB = 6;
+template <bool kGU>
+__host__ __device__ inline int chunk_cost(int n, int nmax) {
+  constexpr int narrow = kGU ? kTokM : kNMaxB;
+  return nmax > narrow ? (n > narrow ? (kGU ? kCostWideA : kCostWideB) : kCostOne) : 1;
 }
 
-// Per-expert down cost: chunk costs of its full and last token tiles and the
-// cost of one H tile row of its token tiles (r).
-struct DownCost {
+// Per-expert cost: chunk costs of its full and last token tiles and the
+// cost of one weight-row tile's token tiles (r).
+struct TileCost {
   int wfull, wlast;
   int64_t r;
 };
-__host__ __device__ inline DownCost down_cost_of(int cnt, int nt, int nmaxB, int kc) {
-  DownCost d;
+template <bool kGU>
+__host__ __device__ inline TileCost tile_cost_of(int cnt, int nt, int nmax, int kc) {
+  TileCost d;
   const int np = (cnt + 15) & ~15;
-  d.wfull = down_chunk_cost(nmaxB, nmaxB);
-  d.wlast = nt > 0 ? down_chunk_cost(np - (nt - 1) * nmaxB, nmaxB) : 0;
+  d.wfull = chunk_cost<kGU>(nmax, nmax);
+  d.wlast = nt > 0 ? chunk_cost<kGU>(np - (nt - 1) * nmax, nmax) : 0;
   d.r = nt > 0 ? (int64_t)kc * ((int64_t)(nt - 1) * d.wfull + d.wlast) : 0;
   return d;
 }
@@ -281,7 +293,7 @@ WR_DEVINL void prefetch_tmap(const CUtensorMap* map) {
 struct BucketArgs {
   const int32_t* ids;  // [TK], written by the routing CTAs of the same launch
   const float* w;
-  int TK, K, ep_first, E, nmaxA, nmaxB, mtA, mtB, kcB;
+  int TK, K, ep_first, E, nmaxA, nmaxB, mtA, mtB, kcA, kcB;
   int* meta;
   int32_t* slot;
   int32_t* row_tok;
@@ -307,7 +319,7 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
   const int32_t* __restrict__ ids = b.ids;
   const float* __restrict__ w = b.w;
   const int TK = b.TK, K = b.K, ep_first = b.ep_first, E = b.E;
-  const int nmaxA = b.nmaxA, nmaxB = b.nmaxB, mtA = b.mtA, mtB = b.mtB, kcB = b.kcB;
+  const int nmaxA = b.nmaxA, nmaxB = b.nmaxB, mtA = b.mtA, mtB = b.mtB, kcA = b.kcA, kcB = b.kcB;
   int* __restrict__ meta = b.meta;
   int32_t* __restrict__ slot = b.slot;
   int32_t* __restrict__ row_tok = b.row_tok;
@@ -365,7 +377,8 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     int* preA = ntlB + E;
     int* preB = preA + E + 1;
     int* costB = preB + E + 1;
-    int b = 0, pa = 0, pb = 0, cb = 0, wmax = 1;
+    int* costA = costB + E + 1;
+    int b = 0, pa = 0, pb = 0, cb = 0, wmax = 1, ca = 0, wmaxA = 1;
     for (int e = 0; e < E; ++e) {
       const int n = s_cnt[e];
       const int np = (n + 15) & ~15;
@@ -379,7 +392,11 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
       s_ntlB[e] = nb;
       preA[e] = pa;
       preB[e] = pb;
-      const DownCost dc = down_cost_of(n, nb, nmaxB, kcB);
+      const TileCost dc = tile_cost_of<false>(n, nb, nmaxB, kcB);
+      const TileCost da = tile_cost_of<true>(n, na, nmaxA, kcA);
+      costA[e] = ca;
+      ca += mtA * (int)da.r;
+      if (na > 0) wmaxA = max(wmaxA, na > 1 ? da.wfull : da.wlast);
       costB[e] = cb;
       s_costB[e] = cb;
       s_rowB[e] = (int)dc.r;
@@ -394,11 +411,14 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     preA[E] = pa;
     preB[E] = pb;
     costB[E] = cb;
+    costA[E] = ca;
     meta[0] = b;
     meta[1] = pa;
     meta[2] = pb;
     meta[3] = cb;
     meta[4] = wmax;
+    meta[5] = ca;
+    meta[6] = wmaxA;
   }
   __syncthreads();
   for (int e = warp; e < E; e += nw) {
@@ -505,51 +525,21 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
 
 // ---------------------------------------------------------------------------
 // Work split (stream-K), both GEMMs: the tiles' K chunks, laid end to end
-// (tile-major), are cut into G equal ranges, one per CTA.  A tile whose
-// chunks straddle several ranges is finished from partial sums: for the
-// down projection each CTA writes an fp32 partial that the combine adds (in
-// CTA order); for gate/up the partial accumulators go to a scratch buffer
-// and the last CTA to finish the tile adds them (in CTA order) and applies
-// SwiGLU.  G is capped so that every range holds at least
-// ceil(kc / (jmax - 1)) chunks, which bounds the CTAs per tile by jmax.
-// SplitK is the gate/up split; the down GEMM cuts ranges of equal cost
-// instead (CostSplit below), which is the same split when every chunk
-// costs the same.
+// (tile-major), chunk (tile, k) at cost position pos(tile) + k * w(tile)
+// (w: chunk_cost), are cut into G ranges of equal cost, one per CTA: CTA c
+// takes the chunks whose position lies in [c C / G, (c + 1) C / G).  A tile
+// whose chunks straddle several ranges is finished from partial sums: for
+// the down projection each CTA writes an fp32 partial that the combine adds
+// (in CTA order); for gate/up the partial accumulators go to a scratch
+// buffer and the last CTA to finish the tile adds them (in CTA order) and
+// applies SwiGLU.  G is capped so that every range holds at least
+// L = ceil(kc / (jmax - 1)) chunks of the dearest kind present, which bounds
+// the CTAs per tile by jmax.
 // ---------------------------------------------------------------------------
-struct SplitK {
-  int64_t U;  // chunks in total
-  int G;      // CTAs with work
-  int kc;     // chunks per tile
-  // CTA whose range holds chunk u: the largest c with floor(c U / G) <= u.
-  WR_DEVINL int cta_of(int64_t u) const { return (int)(((u + 1) * G - 1) / U); }
-  WR_DEVINL int64_t u_lo(int c) const { return (int64_t)c * U / G; }
-  WR_DEVINL int first_cta(int tile) const { return cta_of((int64_t)tile * kc); }
-  WR_DEVINL int last_cta(int tile) const { return cta_of((int64_t)(tile + 1) * kc - 1); }
-  // 0 when `tile` is the first tile CTA c works on, else 1 (it is then c's
-  // last tile): with at most two cut tiles per CTA this names c's partials.
-  WR_DEVINL int part_slot(int c, int tile) const { return u_lo(c) / kc == tile ? 0 : 1; }
-};
-
-WR_DEVINL SplitK make_splitk(int tiles, int kc, int grid, int jmax) {
-  SplitK s;
-  s.U = (int64_t)tiles * kc;
-  s.kc = kc;
-  const int L = (kc + jmax - 2) / (jmax - 1);
-  int64_t g = s.U / L;
-  if (g < 1) g = 1;
-  if (g > grid) g = grid;
-  s.G = (int)g;
-  return s;
-}
-
-// The down split: chunks laid end to end as in SplitK, chunk (tile, k) at
-// cost position pos(tile) + k * w(tile); CTA c takes the chunks whose
-// position lies in [c C / G, (c + 1) C / G).  With all costs 1 this is
-// SplitK.  The grid cap keeps each range >= L chunks of the dearest kind,
-// so a tile still spans at most jmax CTAs.
 struct CostSplit {
   int64_t C;  // total cost
-  int G;
+  int G;      // CTAs with work
+  // CTA whose range holds position p: the largest c with floor(c C / G) <= p.
   WR_DEVINL int cta_of(int64_t p) const { return (int)(((p + 1) * G - 1) / C); }
   WR_DEVINL int64_t lo(int c) const { return (int64_t)c * C / G; }
 };
@@ -716,13 +706,12 @@ struct GemmArgs {
   int kc_total;        // K chunks of kBK per tile (gate/up: over H, down: over I)
   int rmax;            // token rows (padded per expert)
   int wstages, tstages;  // weight ring / token ring depth
-  int tstage_bytes;      // token slot: gate/up nmax rows, down 2 * nmax rows
-  int wide;              // down, nmax 128: a tile uses both accumulators (tokens 0..63, 64..127)
+  int tstage_bytes;      // token slot: gate/up min(nmax, 128) rows, down 2 * nmax rows
   const float* row_w;  // gate/up epilogue: per-row routing weight
   uint16_t* act;       // gate/up output: [2 rmax][I] bf16, rows as act_row_hi / + 16
   float* ypart;        // down output: [jmax][rmax][H] fp32
   int jmax;            // CTAs per tile, at most (gate/up: kJMaxA)
-  float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32
+  float* pbuf;         // gate/up partial accumulators: [CTA][2][nmax][256] fp32 (nmax <= 256)
   uint32_t* cnt;       // gate/up: CTAs done with each cut tile (zeroed by the bucketing)
   uint32_t* status;
 };
@@ -730,12 +719,15 @@ struct GemmArgs {
 // One unit of a CTA's work: weight rows starting at m0 (gate/up: rows
 // m0..m0+127 of gate and of up; down: rows m0..m0+255 of Wd) of expert e
 // against token rows [row0, row0 + n), K chunks [kc0, kc1) taken in the
-// rotated order kc0 + (rot + i) % (kc1 - kc0); j = partial slot (down).
-// The rotation depends only on the tile, so the summation order is fixed;
-// it spreads the CTAs that share a token tile over different K chunks, so
-// they do not all fetch the same L2 lines at the same moment.
+// rotated order kc0 + (rot + i) % (kc1 - kc0); j = partial slot (down);
+// pos, wt = the tile's cost position and chunk cost (the gate/up fixup
+// finds the tile's CTAs from them).  The rotation depends only on the tile,
+// so the summation order is fixed; it spreads the CTAs that share a token
+// tile over different K chunks, so they do not all fetch the same L2 lines
+// at the same moment.
 struct Work {
-  int tile, e, m0, row0, n, kc0, kc1, rot, j;
+  int tile, e, m0, row0, n, kc0, kc1, rot, j, wt;
+  int64_t pos;
   WR_DEVINL int kc_at(int i) const {
     const int len = kc1 - kc0;
     int k = rot + i;
@@ -744,10 +736,11 @@ struct Work {
   }
 };
 
-// The sequence of work one CTA runs (its stream-K chunk range, cut at tile
-// boundaries); every role of the CTA walks the same sequence.  Tiles are
-// numbered expert-major; inside an expert the token tile varies fastest,
-// then the weight-row tile.
+// The sequence of work one CTA runs: the pieces of the tiles whose chunks'
+// cost positions lie in its range, cut at tile boundaries; every role of the
+// CTA walks the same sequence.  Tiles are numbered expert-major; inside an
+// expert the token tile varies fastest, then the weight-row tile.  The grid
+// cap uses the largest chunk cost present, as the down combine does.
 //
 // gate/up: when the range ends inside a tile, that piece runs first.  The
 // CTA holding a tile's last piece sums the tile's partials (the fixup); run
@@ -756,102 +749,74 @@ struct Work {
 // changes no sum: partials are added in CTA order.
 template <bool kGU>
 struct WorkIter {
-  int64_t u, u1;    // the piece sequence being walked
-  int64_t u2, u2e;  // then [u2, u2e) (empty when u2 >= u2e)
-  int e;
-  SplitK sk;
-
-  WR_DEVINL bool init(const GemmArgs& a) {
-    e = 0;
-    sk = make_splitk(__ldg(a.meta + (kGU ? 1 : 2)), a.kc_total, gridDim.x,
-                     a.jmax);
-    if (sk.U == 0 || (int)blockIdx.x >= sk.G) return false;
-    u = sk.u_lo(blockIdx.x);
-    u1 = sk.u_lo(blockIdx.x + 1);
-    u2 = u2e = 0;
-    if (kGU && u < u1 && u1 % sk.kc != 0) {
-      const int64_t lo = ((u1 - 1) / sk.kc) * sk.kc;  // first chunk of the last tile
-      if (lo > u) {  // the end-cut piece [lo, u1) first, then [u, lo)
-        u2 = u;
-        u2e = lo;
-        u = lo;
-      }
-    }
-    return u < u1;
-  }
-
-  WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
-    if (u >= u1) {
-      if (u2 >= u2e) return false;
-      u = u2;
-      u1 = u2e;
-      u2 = u2e = 0;
-      e = 0;  // tiles restart below the piece already walked
-    }
-    const int tile = (int)(u / sk.kc);
-    const int kc0 = (int)(u - (int64_t)tile * sk.kc);
-    const int64_t room = u1 - u;
-    const int len = (int64_t)(sk.kc - kc0) < room ? sk.kc - kc0 : (int)room;
-    w.tile = tile;
-    w.kc0 = kc0;
-    w.kc1 = kc0 + len;
-    w.j = (int)blockIdx.x - sk.first_cta(tile);
-    u += len;
-    const int* pre = kGU ? mv.preA : mv.preB;
-    const int* ntl = kGU ? mv.ntlA : mv.ntlB;
-    while (e + 1 < a.E && __ldg(pre + e + 1) <= tile) ++e;
-    const int local = tile - __ldg(pre + e);
-    const int nt = __ldg(ntl + e);
-    const int tn = local % nt;
-    w.e = e;
-    w.m0 = (local / nt) * (kGU ? kRowsA : kRowsB);
-    const int np = (__ldg(mv.cnt + e) + 15) & ~15;
-    w.row0 = __ldg(mv.base + e) + tn * a.nmax;
-    w.n = min(a.nmax, np - tn * a.nmax);
-    w.rot = (int)(((unsigned)tile * 37u) % (unsigned)len);
-    return true;
-  }
-};
-
-// The down GEMM's sequence: the pieces of the tiles whose chunks' cost
-// positions lie in this CTA's range (CostSplit), in tile order.  The grid
-// cap uses the largest chunk cost present (meta[4]), as the combine does.
-template <>
-struct WorkIter<false> {
   CostSplit cs;
-  SplitK sk;  // not used by the down GEMM (the gate/up fixup's)
-  int64_t p, p1;  // next chunk position to take, end of the range
+  int64_t p, p1;  // next chunk position to take, end of the stretch being walked
+  int64_t q, q1;  // then the stretch [q, q1) (empty when q >= q1)
   int e, m, tn;   // the tile p lies in (or the next one)
 
+  WR_DEVINL const int* cost_prefix(const MetaView& mv) const { return kGU ? mv.costA : mv.costB; }
+  WR_DEVINL int tiles_of(const MetaView& mv, int x) const {
+    return __ldg((kGU ? mv.ntlA : mv.ntlB) + x);
+  }
+
+  // (e, m, tn) = the tile whose cost span holds position x.
+  WR_DEVINL void seek(const GemmArgs& a, const MetaView& mv, int64_t x) {
+    const int* cost = cost_prefix(mv);
+    e = 0;
+    while (e + 1 < a.E && __ldg(cost + e + 1) <= x) ++e;  // experts without tiles cost 0
+    const int nt = tiles_of(mv, e);
+    const TileCost tc = tile_cost_of<kGU>(__ldg(mv.cnt + e), nt, a.nmax, a.kc_total);
+    const int64_t rel = x - __ldg(cost + e);
+    m = (int)(rel / tc.r);
+    tn = (int)((rel - (int64_t)m * tc.r) / ((int64_t)a.kc_total * tc.wfull));
+    if (tn > nt - 1) tn = nt - 1;
+  }
+
+  // Cost position and chunk cost of tile (e, m, tn).
+  WR_DEVINL void tile_pos(const GemmArgs& a, const MetaView& mv, int64_t& pos, int& wt) const {
+    const int nt = tiles_of(mv, e);
+    const TileCost tc = tile_cost_of<kGU>(__ldg(mv.cnt + e), nt, a.nmax, a.kc_total);
+    wt = tn == nt - 1 ? tc.wlast : tc.wfull;
+    pos = __ldg(cost_prefix(mv) + e) + (int64_t)m * tc.r + (int64_t)tn * a.kc_total * tc.wfull;
+  }
+
   WR_DEVINL bool init(const GemmArgs& a) {
-    const int64_t C = __ldg(a.meta + 3);
-    cs = make_costsplit(C, a.kc_total, gridDim.x, a.jmax, __ldg(a.meta + 4));
+    const int64_t C = __ldg(a.meta + (kGU ? 5 : 3));
+    cs = make_costsplit(C, a.kc_total, gridDim.x, a.jmax, __ldg(a.meta + (kGU ? 6 : 4)));
     if (C == 0 || (int)blockIdx.x >= cs.G) return false;
     p = cs.lo(blockIdx.x);
     p1 = cs.lo(blockIdx.x + 1);
+    q = q1 = 0;
     if (p >= p1) return false;
     const MetaView mv = meta_view(a.meta, a.E);
-    e = 0;
-    while (e + 1 < a.E && __ldg(mv.costB + e + 1) <= p) ++e;  // experts without tiles cost 0
-    const int nt = __ldg(mv.ntlB + e);
-    const DownCost dc = down_cost_of(__ldg(mv.cnt + e), nt, a.nmax, a.kc_total);
-    const int64_t rel = p - __ldg(mv.costB + e);
-    m = (int)(rel / dc.r);
-    tn = (int)((rel - (int64_t)m * dc.r) / ((int64_t)a.kc_total * dc.wfull));
-    if (tn > nt - 1) tn = nt - 1;
+    if (kGU) {
+      // the tile holding the range's last position: if the range ends inside
+      // it and it is not the range's first tile, walk [its start, p1) first
+      seek(a, mv, p1 - 1);
+      int64_t pos;
+      int wt;
+      tile_pos(a, mv, pos, wt);
+      const int64_t k1 = (p1 - pos + wt - 1) / wt;
+      if (k1 < a.kc_total && pos > p) {
+        q = p;
+        q1 = pos;
+        p = pos;
+        return true;
+      }
+    }
+    seek(a, mv, p);
     return true;
   }
 
-  WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
+  // The next piece of the stretch [p, p1), or false at its end.
+  WR_DEVINL bool take(const GemmArgs& a, const MetaView& mv, Work& w) {
     const int kc = a.kc_total;
-    const int mt = (a.H + kRowsB - 1) / kRowsB;
+    const int mt = kGU ? (a.I + kRowsA - 1) / kRowsA : (a.H + kRowsB - 1) / kRowsB;
     while (p < p1 && e < a.E) {
-      const int nt = __ldg(mv.ntlB + e);
-      const int cnt = __ldg(mv.cnt + e);
-      const DownCost dc = down_cost_of(cnt, nt, a.nmax, kc);
-      const int wt = tn == nt - 1 ? dc.wlast : dc.wfull;
-      const int64_t pos =
-          __ldg(mv.costB + e) + (int64_t)m * dc.r + (int64_t)tn * kc * dc.wfull;
+      const int nt = tiles_of(mv, e);
+      int64_t pos;
+      int wt;
+      tile_pos(a, mv, pos, wt);
       const int64_t k0 = p > pos ? (p - pos + wt - 1) / wt : 0;
       int64_t k1 = (p1 - pos + wt - 1) / wt;
       if (k1 > kc) k1 = kc;
@@ -862,30 +827,102 @@ struct WorkIter<false> {
           m = 0;
           do {
             ++e;
-          } while (e < a.E && __ldg(mv.ntlB + e) == 0);
+          } while (e < a.E && tiles_of(mv, e) == 0);
         }
       }
       if (k0 >= kc) continue;  // p is past this tile's last chunk
-      if (k1 <= k0) {
-        p = p1;
-        return false;
-      }
+      if (k1 <= k0) break;
       p = pos + k1 * wt;
-      w.tile = __ldg(mv.preB + ce) + cm * nt + ctn;
+      w.tile = __ldg((kGU ? mv.preA : mv.preB) + ce) + cm * nt + ctn;
       w.kc0 = (int)k0;
       w.kc1 = (int)k1;
       w.j = (int)blockIdx.x - cs.cta_of(pos);
       w.e = ce;
-      w.m0 = cm * kRowsB;
-      const int np = (cnt + 15) & ~15;
+      w.m0 = cm * (kGU ? kRowsA : kRowsB);
+      const int np = (__ldg(mv.cnt + ce) + 15) & ~15;
       w.row0 = __ldg(mv.base + ce) + ctn * a.nmax;
       w.n = min(a.nmax, np - ctn * a.nmax);
       w.rot = (int)(((unsigned)w.tile * 37u) % (unsigned)(k1 - k0));
+      w.pos = pos;
+      w.wt = wt;
       return true;
     }
+    p = p1;
     return false;
   }
+
+  WR_DEVINL bool next(const GemmArgs& a, const MetaView& mv, Work& w) {
+    for (;;) {
+      if (take(a, mv, w)) return true;
+      if (q >= q1) return false;
+      p = q;
+      p1 = q1;
+      q = q1 = 0;
+      seek(a, mv, p);
+    }
+  }
+
+  // The CTAs holding pieces of tile w: first and last.
+  WR_DEVINL int first_cta(const Work& w) const { return cs.cta_of(w.pos); }
+  WR_DEVINL int last_cta(const GemmArgs& a, const Work& w) const {
+    return cs.cta_of(w.pos + (int64_t)(a.kc_total - 1) * w.wt);
+  }
 };
+
+// gate/up partial slots: a CTA has at most two cut tiles, the one its range
+// starts in (its piece starts after chunk 0) and the one its range ends in
+// (its piece starts at chunk 0: the tile's first CTA); slot 1 is the latter.
+WR_DEVINL int part_slot_of_piece(const Work& w) { return w.kc0 == 0 ? 1 : 0; }
+WR_DEVINL int part_slot_of_cta(int c, int first) { return c == first ? 1 : 0; }
+
+// TMEM accumulators: two buffers of 256 columns.  A tile of at most 128
+// tokens (gate/up) or 64 tokens (down) takes one buffer, the two in turn, so
+// the epilogue of one tile overlaps the MMAs of the next; a wider tile takes
+// both (its tokens 128.. / 64.. in the second).  The MMA lane and the
+// epilogue warps walk the same tiles and derive the same buffers and phases.
+struct AccTurns {
+  uint32_t use0, use1;  // uses of buffer 0 / 1 so far
+  int next;
+  WR_DEVINL void init() {
+    use0 = use1 = 0u;
+    next = 0;
+  }
+  // This tile's buffers [b0, b0 + nb) and each one's phase for this use.
+  WR_DEVINL void take(bool wide, int& b0, int& nb, uint32_t (&ph)[2]) {
+    if (wide) {
+      b0 = 0;
+      nb = 2;
+      ph[0] = use0++ & 1u;
+      ph[1] = use1++ & 1u;
+      next = 0;
+    } else if (next == 0) {
+      b0 = 0;
+      nb = 1;
+      ph[0] = use0++ & 1u;
+      next = 1;
+    } else {
+      b0 = 1;
+      nb = 1;
+      ph[0] = use1++ & 1u;
+      next = 0;
+    }
+  }
+};
+
+// An epilogue warp is done reading buffers [b0, b0 + nb): one arrival each.
+WR_DEVINL void release_acc(uint64_t* tempty, int b0, int nb, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_arrive(&tempty[b0]);
+    if (nb > 1) mbar_arrive(&tempty[b0 + 1]);
+  }
+}
+
+template <bool kGU>
+WR_DEVINL bool tile_is_wide(const Work& w) {
+  return w.n > (kGU ? kTokM : kNMaxB);
+}
 
 WR_DEVINL void flag_timeout(const GemmArgs& a, volatile int* abort, uint32_t bit) {
   *abort = 1;
@@ -1051,40 +1088,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       Work w;
       while (ok && it.next(a, mv, w)) {
         const int nbox = w.n / kBoxRows;
-        const uint32_t bytes =
-            wprod ? (uint32_t)kWStageBytes : (uint32_t)((kGU ? 1 : 2) * w.n * kRowB);
-        for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+        // a gate/up tile of more than 128 tokens takes two token slots per K
+        // step: rows 0..127, then rows 128.. (each slot one MMA's A operand)
+        const bool split = kGU && !wprod && w.n > kTokM;
+        for (int i = 0; i < w.kc1 - w.kc0 && ok; ++i) {
           const int kc = w.kc_at(i);
-          if (!mbar_wait(&empty[st], ph ^ 1u, abort)) {
-            if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_EMPTY);
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[st], bytes);
-          uint8_t* s = ring + (size_t)st * sbytes;
           const int kx = kc * kBK;
-          if (wprod) {
-            // gate/up: gate rows m0.. then up rows m0..; down: Wd rows m0..m0+255
-            tma_load_3d(s, &tm_w, kx, w.m0, w.e, &full[st], pol);
-            tma_load_3d(s + kWBox * kRowB, &tm_w, kx, kGU ? a.I + w.m0 : w.m0 + kWBox, w.e,
-                        &full[st], pol);
-          } else {
-            // gate/up: the tile's n token rows; down: its 2n activation rows
-            // (act_hi / act_lo blocks of 16, row0 a multiple of 16)
-            if (kGU)
-              tma_load_2d(s, &tm_b.m[nbox - 1], kx, w.row0, &full[st], pol);
-            else {  // at most 128 rows per box: a wide tile's tokens 64.. in a second box
+          for (int h = 0; h < (split ? 2 : 1); ++h) {
+            if (!mbar_wait(&empty[st], ph ^ 1u, abort)) {
+              if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_EMPTY);
+              ok = false;
+              break;
+            }
+            uint8_t* s = ring + (size_t)st * sbytes;
+            if (wprod) {
+              // gate/up: gate rows m0.. then up rows m0..; down: Wd rows m0..m0+255
+              mbar_arrive_expect_tx(&full[st], (uint32_t)kWStageBytes);
+              tma_load_3d(s, &tm_w, kx, w.m0, w.e, &full[st], pol);
+              tma_load_3d(s + kWBox * kRowB, &tm_w, kx, kGU ? a.I + w.m0 : w.m0 + kWBox, w.e,
+                          &full[st], pol);
+            } else if (kGU) {
+              // the tile's token rows (one half of a split tile)
+              const int nb = split ? (h == 0 ? kTokMaps : nbox - kTokMaps) : nbox;
+              mbar_arrive_expect_tx(&full[st], (uint32_t)(nb * kBoxRows * kRowB));
+              tma_load_2d(s, &tm_b.m[nb - 1], kx, w.row0 + h * kTokM, &full[st], pol);
+            } else {
+              // its 2n activation rows (act_hi / act_lo blocks of 16, row0 a
+              // multiple of 16), at most 128 rows per box: a wide tile's
+              // tokens 64.. in a second box
+              mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * w.n * kRowB));
               const int b0 = nbox < kTokMaps / 2 ? nbox : kTokMaps / 2;
               tma_load_2d(s, &tm_b.m[2 * b0 - 1], kx, 2 * w.row0, &full[st], pol);
               if (nbox > b0)
                 tma_load_2d(s + kTokBytes, &tm_b.m[2 * (nbox - b0) - 1], kx,
                             2 * w.row0 + kTokM, &full[st], pol);
             }
-          }
-          ++issued;
-          if (++st == stages) {
-            st = 0;
-            ph ^= 1u;
+            ++issued;
+            if (++st == stages) {
+              st = 0;
+              ph ^= 1u;
+            }
           }
         }
       }
@@ -1095,53 +1138,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int sw = 0, stt = 0;
       uint32_t phw = 0, pht = 0;
-      int j = 0;
       bool ok = true;
       const uint32_t idesc = idesc_bf16(kTokM, kWRows);
       WorkIter<kGU> it;
       it.init(a);
       Work w;
-      for (; ok && it.next(a, mv, w); ++j) {
-        // two accumulator buffers in turn, or (wide tiles) one of 512 columns
-        const int ab = a.wide ? 0 : (j & 1);
-        const uint32_t aph = a.wide ? (uint32_t)(j & 1) : (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(&tempty[ab], aph ^ 1u, abort)) {
-          if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
-          break;
-        }
+      AccTurns acc;
+      acc.init();
+      while (ok && it.next(a, mv, w)) {
+        const bool wide = tile_is_wide<kGU>(w);
+        int b0, nb;
+        uint32_t aph[2];
+        acc.take(wide, b0, nb, aph);
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+          if (b < nb && ok && !mbar_wait(&tempty[b0 + b], aph[b] ^ 1u, abort)) {
+            if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
+            ok = false;
+          }
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(ab * kAccStride);
+        const uint32_t d = tmem_base + (uint32_t)(b0 * kAccStride);
         for (int i = 0; i < w.kc1 - w.kc0; ++i) {
           if (!mbar_wait(&fullW[sw], phw, abort) || !mbar_wait(&fullT[stt], pht, abort)) {
             if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
             ok = false;
             break;
           }
+          // a wide gate/up tile's tokens 128.. are in the next token slot; a
+          // wide down tile's tokens 64.. (A rows 128..) in the same slot
+          int st2 = stt;
+          uint32_t ph2 = pht;
+          if (kGU && wide) {
+            if (++st2 == a.tstages) {
+              st2 = 0;
+              ph2 ^= 1u;
+            }
+            if (!mbar_wait(&fullT[st2], ph2, abort)) {
+              if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
+              ok = false;
+              break;
+            }
+          }
           tc_fence_after();
           const uint32_t sw_addr = smem_u32(smem + (size_t)sw * kWStageBytes);
           const uint32_t st_addr = smem_u32(tring + (size_t)stt * a.tstage_bytes);
+          const uint32_t st2_addr =
+              kGU ? smem_u32(tring + (size_t)st2 * a.tstage_bytes) : st_addr + kTokBytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
             const uint64_t wdesc = sw128_desc(sw_addr + kk * 32);
-            umma_bf16(d, sw128_desc(st_addr + kk * 32), wdesc, idesc, acc);
-            if (!kGU && w.n > kNMaxB)  // tokens 64.. (A rows 128..) into the second accumulator
-              umma_bf16(d + kAccStride, sw128_desc(st_addr + kTokBytes + kk * 32), wdesc, idesc,
-                        acc);
+            umma_bf16(d, sw128_desc(st_addr + kk * 32), wdesc, idesc, accum);
+            if (wide)
+              umma_bf16(d + kAccStride, sw128_desc(st2_addr + kk * 32), wdesc, idesc, accum);
           }
           umma_commit(&emptyW[sw]);
           umma_commit(&emptyT[stt]);
+          if (kGU && wide) umma_commit(&emptyT[st2]);
           if (++sw == a.wstages) {
             sw = 0;
             phw ^= 1u;
           }
+          stt = st2;
+          pht = ph2;
           if (++stt == a.tstages) {
             stt = 0;
             pht ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[ab]);
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+          if (b < nb) umma_commit(&tfull[b0 + b]);
       }
       // Every MMA issued above must complete before TMEM is released.
       umma_commit(drain);
@@ -1150,38 +1219,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---- epilogue: warps 2..5, TMEM lane quarter warp % 4 ----
     const int q = warp & 3;
-    int j = 0;
     WorkIter<kGU> it;
     it.init(a);
     Work w;
-    for (; it.next(a, mv, w); ++j) {
-      const int ab = a.wide ? 0 : (j & 1);
-      const uint32_t aph = a.wide ? (uint32_t)(j & 1) : (uint32_t)(j >> 1) & 1u;
+    AccTurns acc;
+    acc.init();
+    while (it.next(a, mv, w)) {
+      int b0, nb;
+      uint32_t aph[2];
+      acc.take(tile_is_wide<kGU>(w), b0, nb, aph);
       bool bad = *abort != 0;
-      if (!bad && !mbar_wait(&tfull[ab], aph, abort)) {
-        if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_ACT);
-        bad = true;
-      }
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+        if (b < nb && !bad && !mbar_wait(&tfull[b0 + b], aph[b], abort)) {
+          if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_ACT);
+          bad = true;
+        }
       // The four epilogue warps leave together or not at all: the down
       // epilogue synchronises them on a named barrier.
       if (named_bar_or(2, 128, bad)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kAccStride);
+      const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b0 * kAccStride);
       if (kGU) {
-        // lane = token t of the tile; columns c / 128 + c = gate / up row m0 + c
-        const int t = 32 * q + lane;
-        const bool has = 32 * q < w.n;  // warp-uniform: this quarter holds tokens
-        const bool live = t < w.n;
-        const int r = w.row0 + t;
-        uint16_t* hi = a.act + act_row_hi(r) * a.I;
-        uint16_t* lo = hi + 16 * (int64_t)a.I;
-        if (w.kc0 == 0 && w.kc1 == a.kc_total) {  // whole tile in this CTA
-          if (has) {
+        // lane = token t of the tile (buffer h holds tokens 128h..); columns
+        // c / 128 + c = gate / up row m0 + c
+        const bool whole = w.kc0 == 0 && w.kc1 == a.kc_total;  // whole tile in this CTA
+        for (int h = 0; h < nb; ++h) {
+          const int t = kTokM * h + 32 * q + lane;
+          if (t - lane >= w.n) continue;  // warp-uniform: this quarter holds no tokens
+          const bool live = t < w.n;
+          const uint32_t tb = taddr + (uint32_t)(h * kAccStride);
+          if (whole) {
+            const int r = w.row0 + t;
+            uint16_t* hi = a.act + act_row_hi(r) * a.I;
+            uint16_t* lo = hi + 16 * (int64_t)a.I;
             const float wt = live ? __ldg(a.row_w + r) : 0.0f;
             for (int c0 = 0; c0 < kRowsA; c0 += 16) {
               uint32_t gv[16], uv[16];
-              tmem_ld16(taddr + c0, gv);
-              tmem_ld16(taddr + kRowsA + c0, uv);
+              tmem_ld16(tb + c0, gv);
+              tmem_ld16(tb + kRowsA + c0, uv);
               tmem_wait_ld(gv);
               reg_dep16(uv);
               float g[16], u[16];
@@ -1192,18 +1268,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
               if (live) swiglu_store16(g, u, wt, hi, lo, w.m0 + c0, a.I);
             }
-          }
-        } else {
-          // Cut tile: park this CTA's partial sums, count it in; the last
-          // CTA of the tile adds the partials in CTA order and applies SwiGLU.
-          const SplitK& sk = it.sk;
-          float* pb = a.pbuf +
-                      (((size_t)blockIdx.x * 2 + sk.part_slot(blockIdx.x, w.tile)) * a.nmax + t) *
-                          kWRows;
-          if (has) {
+          } else {
+            // Cut tile: park this CTA's partial sums (below: count it in; the
+            // last CTA of the tile adds the partials in CTA order and applies
+            // SwiGLU).
+            float* pb =
+                a.pbuf +
+                (((size_t)blockIdx.x * 2 + part_slot_of_piece(w)) * a.nmax + t) *
+                    kWRows;
             for (int c0 = 0; c0 < kWRows; c0 += 16) {
               uint32_t v[16];
-              tmem_ld16(taddr + c0, v);
+              tmem_ld16(tb + c0, v);
               tmem_wait_ld(v);
               if (live) {
 #pragma unroll
@@ -1214,9 +1289,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
           }
+        }
+        // The accumulators are read: hand them back to the MMA lane before
+        // the fixup below, so the next tile's MMAs overlap it.
+        release_acc(tempty, b0, nb, lane);
+        if (!whole) {
           __threadfence();
           named_bar_sync(1, 128);
-          const int cf = sk.first_cta(w.tile), cl = sk.last_cta(w.tile);
+          const int cf = it.first_cta(w), cl = it.last_cta(a, w);
           if (threadIdx.x == 64) {
             const uint32_t done = atomicAdd(&a.cnt[w.tile], 1u);
             *last_flag = done == (uint32_t)(cl - cf) ? 1 : 0;
@@ -1238,7 +1318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int cc = 0; cc < kJMaxA; ++cc) {
                 if (cf + cc <= cl) {
                   const float* src = a.pbuf + (((size_t)(cf + cc) * 2 +
-                                                sk.part_slot(cf + cc, w.tile)) * a.nmax + tt) *
+                                                part_slot_of_cta(cf + cc, cf)) * a.nmax + tt) *
                                                   kWRows;
 #pragma unroll
                   for (int k = 0; k < 4; ++k) {
@@ -1303,9 +1383,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[ab]);
+      if (!kGU) release_acc(tempty, b0, nb, lane);
     }
   }
 
@@ -1417,14 +1495,14 @@ GroupedPlan make_plan(const Problem& p) {
   GroupedPlan g;
   const int TK = p.T * p.K;
   const int n16 = (p.T + 15) & ~15;
-  g.nmaxA = n16 < kNMaxA ? n16 : kNMaxA;
+  g.nmaxA = n16 <= kNMaxA ? n16 : kNMaxAWide;
   g.nmaxB = n16 <= kNMaxB ? n16 : kNMaxBWide;
   g.rmax = (TK + 15 * p.ep_num + 15) & ~15;
   g.mtA = (p.I + kRowsA - 1) / kRowsA;
   g.mtB = (p.H + kRowsB - 1) / kRowsB;
   g.kcA = (p.H + kBK - 1) / kBK;
   g.kcB = (p.I + kBK - 1) / kBK;
-  g.tbA = g.nmaxA * kRowB;
+  g.tbA = (g.nmaxA < kTokM ? g.nmaxA : kTokM) * kRowB;  // a wide tile takes two slots
   g.tbB = 2 * g.nmaxB * kRowB;
   ring_split(g.tbA, kSmemBase, &g.wstA, &g.tstA);
   ring_split(g.tbB, kSmemBase, &g.wstB, &g.tstB);
@@ -1528,6 +1606,7 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ba.nmaxB = g.nmaxB;
   ba.mtA = g.mtA;
   ba.mtB = g.mtB;
+  ba.kcA = g.kcA;
   ba.kcB = g.kcB;
   ba.meta = meta;
   ba.slot = slot;
@@ -1592,7 +1671,6 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ga.cnt = tcnt;
   ga.status = status;
 
-  ga.wide = 0;
   GemmArgs a1 = ga;
   a1.nmax = g.nmaxA;
   a1.kc_total = g.kcA;
@@ -1612,7 +1690,6 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   a2.wstages = g.wstB;
   a2.tstages = g.tstB;
   a2.tstage_bytes = g.tbB;
-  a2.wide = g.nmaxB > kNMaxB;
   const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB +
                        kSmemBase;
   ce = launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream, tm_dn,
