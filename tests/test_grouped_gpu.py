@@ -208,12 +208,56 @@ def test_deterministic_and_workspace_reusable():
     assert torch.equal(a, b)
 
 
-def test_fp32_batches_keep_the_streaming_path():
-    E, H, I, K, T = 8, 512, 1024, 2, 20
+@pytest.mark.parametrize("E,H,I,K,T", [
+    (8, 512, 1024, 2, 20),     # the smallest shapes
+    (8, 1000, 1000, 2, 37),    # row tiles and K chunks with tails (TMA zero fill)
+    (4, 1024, 1536, 4, 64),    # top_k 4: experts with up to 64 tokens, one tile each
+    (8, 1024, 2048, 2, 130),   # experts with several 64-token tiles
+    (64, 256, 128, 8, 40),     # the most experts, top_k 8: many small buckets
+    (8, 512, 1024, 2, 5),      # the smallest fp32 batch on the grouped path
+])
+def test_fp32_batches_grouped(E, H, I, K, T):
+    """fp32 batches (warp-route's dtype) on the tensor cores: weights split
+    into bf16 hi + lo in shared memory, tokens and activations likewise."""
     L = synthetic.make_layer(E, H, I, K, dtype=torch.float32, seed=31, tokens=T)
     out, ids, w = _run(L, E, H, I, K)
     _check_routing(ids, w, L, K)
     _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, list(range(T)))
+
+
+def test_fp32_hot_expert_and_expert_shards():
+    """fp32: a bias sends every token to expert 1 first (150 tokens: three
+    token tiles, nearly every tile cut between CTAs), and four expert shards
+    sum to the whole layer."""
+    E, H, I, K, T = 8, 1024, 2048, 2, 150
+    bias = torch.zeros(E, dtype=torch.float32, device="cuda")
+    bias[1] = 50.0
+    full = synthetic.make_layer(E, H, I, K, dtype=torch.float32, seed=41, tokens=T)
+    ref, ids, _ = abi_layer(full.x, full.gate_w, full.weight_buf, E, H, I, K, bias=bias)
+    torch.cuda.synchronize()
+    assert (ids[:, 0] == 1).all()
+    _check_rows(ref, full.x, full.gate_w, full.weight_buf, E, H, I, K, [0, 63, 64, 127, 149],
+                bias)
+    acc = torch.zeros_like(ref)
+    for r in range(4):
+        sh = synthetic.make_layer(E, H, I, K, dtype=torch.float32, seed=41, tokens=T,
+                                  ep_rank=r, ep_size=4)
+        out, _, _ = abi_layer(sh.x, sh.gate_w, sh.weight_buf, E, H, I, K, bias=bias,
+                              ep_first=sh.ep_first, ep_num=sh.ep_num)
+        acc += out
+    torch.cuda.synchronize()
+    assert oracle.rel_l2(acc.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+
+
+def test_fp32_mixtral_shape_batch():
+    """The Mixtral shape in fp32 at T = 16 with the sweep's router bias."""
+    E, H, I, K = synthetic.SHAPES["mixtral"]
+    T = 16
+    L = synthetic.make_layer(E, H, I, K, dtype=torch.float32, seed=43, tokens=T,
+                             router_bias=True)
+    out, ids, w = _run(L, E, H, I, K)
+    _check_routing(ids, w, L, K)
+    _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, 7, 15], L.router_bias)
 
 
 def test_python_api_matches_c_abi():

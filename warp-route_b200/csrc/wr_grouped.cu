@@ -453,8 +453,9 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
 constexpr int kRouteThreads = 32 * kRouterSegments;
 constexpr int kCtlRoute = 4;  // control word: routing CTAs done (zero between launches)
 
+template <typename Tx>
 __global__ void __launch_bounds__(kRouteThreads) k_route_bucket(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ gate_w,
+    const Tx* __restrict__ x, const Tx* __restrict__ gate_w,
     const float* __restrict__ bias, int E_all, int H, bool vec_ok, uint32_t* __restrict__ ctl,
     int32_t* __restrict__ ids_out, float* __restrict__ w_out, const BucketArgs b) {
   extern __shared__ int s_dyn[];
@@ -468,16 +469,16 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_bucket(
   // on that kernel and x may, but a prefetch into L2, the point of
   // coherence, cannot make a later read return stale data.
   if (threadIdx.x == 0 && vec_ok) {
-    prefetch_share_l2(gate_w, (int64_t)E_all * H * 2, blockIdx.x, gridDim.x);
-    prefetch_share_l2(x + (int64_t)blockIdx.x * H, (int64_t)H * 2, 0, 1);
+    prefetch_share_l2(gate_w, (int64_t)E_all * H * sizeof(Tx), blockIdx.x, gridDim.x);
+    prefetch_share_l2(x + (int64_t)blockIdx.x * H, (int64_t)H * sizeof(Tx), 0, 1);
   }
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = b.K;
-  router_segment_warp<uint16_t>(gate_w, XGlobal<uint16_t>{x + (int64_t)t * H}, E_all, H, warp,
-                                lane, vec_ok, parts + warp * kMaxExperts);
+  router_segment_warp<Tx>(gate_w, XGlobal<Tx>{x + (int64_t)t * H}, E_all, H, warp, lane, vec_ok,
+                          parts + warp * kMaxExperts);
   __syncthreads();
   for (int e = threadIdx.x; e < E_all; e += blockDim.x)
     lg[e] = router_combine(parts, kMaxExperts, e, bias);
@@ -523,6 +524,50 @@ __global__ void __launch_bounds__(256) k_gather(const uint4* __restrict__ x, int
   }
 }
 
+// Activation rows: token row r's act_hi is row act_row_hi(r) and its act_lo
+// 16 rows further: blocks of 16 act_hi rows, each followed by the same 16
+// tokens' act_lo rows.  A down tile's 2n rows are then one TMA box per 64
+// tokens, and as an MMA's A rows they put token t's two halves (t < 64) in
+// accumulator lanes 32q + l and 32q + 16 + l (q = t / 16, l = t % 16): the
+// same warp, 16 lanes apart.
+WR_DEVINL int64_t act_row_hi(int r) { return 2 * (int64_t)(r & ~15) + (r & 15); }
+
+// fp32 tokens: X_g holds each row split into bf16 hi = rn(x) and lo =
+// rn(x - hi), laid out like the activations (act_row_hi): blocks of 16 hi
+// rows, each followed by the same 16 rows' lo parts; zero for padding.
+__global__ void __launch_bounds__(256) k_gather_f32(const float4* __restrict__ x, int H8,
+                                                    const int* __restrict__ meta,
+                                                    const int32_t* __restrict__ row_tok,
+                                                    uint4* __restrict__ xg) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int rows = meta[0];
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int t = row_tok[r];
+    uint4* hi = xg + act_row_hi(r) * H8;
+    uint4* lo = hi + 16 * (int64_t)H8;
+    for (int c = threadIdx.x; c < H8; c += blockDim.x) {
+      if (t < 0) {
+        hi[c] = lo[c] = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      const float4 a = x[((int64_t)t * H8 + c) * 2], b = x[((int64_t)t * H8 + c) * 2 + 1];
+      const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t ph[4], pl[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * k]), h1 = __float2bfloat16_rn(v[2 * k + 1]);
+        ph[k] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(v[2 * k] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(v[2 * k + 1] - __bfloat162float(h1));
+        pl[k] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+      }
+      hi[c] = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+      lo[c] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Work split (stream-K), both GEMMs: the tiles' K chunks, laid end to end
 // (tile-major), chunk (tile, k) at cost position pos(tile) + k * w(tile)
@@ -561,15 +606,16 @@ __global__ void __launch_bounds__(256) k_combine(const float4* __restrict__ ypar
                                                  const int32_t* __restrict__ slot,
                                                  const int4* __restrict__ row_tile,
                                                  const int* __restrict__ meta, int K, int H4,
-                                                 int rmax, int kcB, int grid, int jmax,
-                                                 const Residual res, float4* __restrict__ out) {
+                                                 int rmax, int kcB, int rowsB, int grid,
+                                                 int jmax, const Residual res,
+                                                 float4* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   const int h = blockIdx.y * blockDim.x + threadIdx.x;
   if (h >= H4) return;
   const CostSplit cs = make_costsplit(meta[3], kcB, grid, jmax, meta[4]);
-  const int mt = (h * 4) / kRowsB;
+  const int mt = (h * 4) / rowsB;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
     const int r = slot[(int64_t)t * K + k];
@@ -610,8 +656,8 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
                                                     const int32_t* __restrict__ slot,
                                                     const int4* __restrict__ row_tile,
                                                     const int* __restrict__ meta, int K, int H,
-                                                    int rmax, int kcB, int grid, int jmax,
-                                                    int t0,
+                                                    int rmax, int kcB, int rowsB, int grid,
+                                                    int jmax, int t0,
                                                     int Tc, const CommView comm,
                                                     const Residual res,
                                                     uint32_t* __restrict__ ctl,
@@ -630,7 +676,7 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
   for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += stride) {
     const int tl = it / H4, h4 = it - tl * H4;
     const int t = t0 + tl;
-    const int mt = (h4 * 4) / kRowsB;
+    const int mt = (h4 * 4) / rowsB;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
       const int r = slot[(int64_t)t * K + k];
@@ -704,6 +750,7 @@ struct GemmArgs {
   int H, I;
   int nmax;            // token rows per tile
   int kc_total;        // K chunks of kBK per tile (gate/up: over H, down: over I)
+  int mrows;           // weight rows per tile (gate/up: of gate and of up; down: of Wd)
   int rmax;            // token rows (padded per expert)
   int wstages, tstages;  // weight ring / token ring depth
   int tstage_bytes;      // token slot: gate/up min(nmax, 128) rows, down 2 * nmax rows
@@ -811,7 +858,7 @@ struct WorkIter {
   // The next piece of the stretch [p, p1), or false at its end.
   WR_DEVINL bool take(const GemmArgs& a, const MetaView& mv, Work& w) {
     const int kc = a.kc_total;
-    const int mt = kGU ? (a.I + kRowsA - 1) / kRowsA : (a.H + kRowsB - 1) / kRowsB;
+    const int mt = ((kGU ? a.I : a.H) + a.mrows - 1) / a.mrows;
     while (p < p1 && e < a.E) {
       const int nt = tiles_of(mv, e);
       int64_t pos;
@@ -838,7 +885,7 @@ struct WorkIter {
       w.kc1 = (int)k1;
       w.j = (int)blockIdx.x - cs.cta_of(pos);
       w.e = ce;
-      w.m0 = cm * (kGU ? kRowsA : kRowsB);
+      w.m0 = cm * a.mrows;
       const int np = (__ldg(mv.cnt + ce) + 15) & ~15;
       w.row0 = __ldg(mv.base + ce) + ctn * a.nmax;
       w.n = min(a.nmax, np - ctn * a.nmax);
@@ -950,13 +997,6 @@ WR_DEVINL uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
   return (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
 }
 
-// Activation rows: token row r's act_hi is row act_row_hi(r) and its act_lo
-// 16 rows further: blocks of 16 act_hi rows, each followed by the same 16
-// tokens' act_lo rows.  A down tile's 2n rows are then one TMA box per 64
-// tokens, and as an MMA's A rows they put token t's two halves (t < 64) in
-// accumulator lanes 32q + l and 32q + 16 + l (q = t / 16, l = t % 16): the
-// same warp, 16 lanes apart.
-WR_DEVINL int64_t act_row_hi(int r) { return 2 * (int64_t)(r & ~15) + (r & 15); }
 
 // act = silu(g) * u * wt for 16 consecutive intermediate rows i.. of one
 // token, stored as bf16 hi (act rounded) and lo (act - hi rounded).
@@ -1397,6 +1437,449 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// fp32 weights (warp-route's own dtype) on the same tensor cores.  The MMAs
+// take bf16 operands, so every fp32 value v is split into hi = rn(v) and
+// lo = rn(v - hi) (together exact to about 2^-17 relative):
+//   * tokens and activations: hi and lo rows interleaved in blocks of 16
+//     (act_row_hi), so one MMA's 128 A rows hold 64 tokens' hi and lo parts
+//     in accumulator lanes 32q + l and 32q + 16 + l, added by one shuffle;
+//   * weights: the fp32 rows land in shared memory by TMA (two 128-byte
+//     swizzled boxes of 32 K elements per stage) and four converter warps
+//     write their hi and lo parts as two bf16 stages in the MMA layout.
+// Per K step of 16: D += A x W_hi, D += A x W_lo (N = 128 weight rows), so D
+// holds (x_hi + x_lo) . (w_hi + w_lo) summed in fp32.  Tiles: gate/up 64
+// gate + 64 up rows (accumulator columns 0..63 / 64..127), down 128 rows of
+// Wd; at most 64 tokens per tile.  The weights stream from HBM once per
+// batch; each byte of them is read by the TMA and once more by a converter.
+// ---------------------------------------------------------------------------
+constexpr int kF32Rows = 128;                     // weight rows per stage and MMA N
+constexpr int kRowsAF = 64;                       // gate/up tile: rows of gate and of up
+constexpr int kRowsBF = 128;                      // down tile: rows of Wd
+constexpr int kNMaxF = 64;                        // tokens per tile
+constexpr int kLStageBytes = kF32Rows * kBK * 4;  // 32 KB fp32 landing stage: two K halves
+constexpr int kLHalfBytes = kLStageBytes / 2;     // 128 rows x 32 fp32 (128-byte rows)
+constexpr int kCHalfBytes = kF32Rows * kRowB;     // 16 KB: 128 bf16 rows of 64 K
+constexpr int kCStageBytes = 2 * kCHalfBytes;     // hi rows, then lo rows
+constexpr int kLStagesF = 4, kCStagesF = 2, kTStagesF = 2;
+constexpr int kConvWarps = 4;                     // warps 7..10
+constexpr int kConvRows = 8;                      // rows a converter lane has in flight
+constexpr int kGemmThreadsF = 32 * (7 + kConvWarps);
+constexpr int kTmemColsF = 256;                   // two accumulators of 128 columns
+constexpr int kAccStrideF = 128;
+constexpr int kSmemF = kTStagesF * kTokBytes + kLStagesF * kLStageBytes +
+                       kCStagesF * kCStageBytes + kSmemBase;
+static_assert(kSmemF <= kSmemMax, "fp32 grouped GEMM shared memory");
+static_assert((2 * kLStagesF + 2 * kCStagesF + 2 * kTStagesF + 5) * 8 + 12 <= 512, "barriers");
+
+// act = silu(g) * u * wt for 8 consecutive intermediate rows i.. of one
+// token (i a multiple of 8, I a multiple of 8), stored as bf16 hi and lo.
+WR_DEVINL void swiglu_store8(const float (&g)[8], const float (&u)[8], float wt, uint16_t* hi,
+                             uint16_t* lo, int i, int I) {
+  if (i >= I) return;
+  uint32_t ph[4], pl[4];
+#pragma unroll
+  for (int c = 0; c < 8; c += 2) {
+    float av[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) av[k] = silu_fast(g[c + k]) * u[c + k] * wt;
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(av[0]);
+    const __nv_bfloat16 h1 = __float2bfloat16_rn(av[1]);
+    ph[c / 2] = pack_bf16x2(h0, h1);
+    pl[c / 2] = pack_bf16x2(__float2bfloat16_rn(av[0] - __bfloat162float(h0)),
+                            __float2bfloat16_rn(av[1] - __bfloat162float(h1)));
+  }
+  *reinterpret_cast<uint4*>(hi + i) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+  *reinterpret_cast<uint4*>(lo + i) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+}
+
+// The 16 columns c0.. of this lane's accumulator row, hi and lo lanes added:
+// lanes l < 16 get columns c0..c0+7, lanes l + 16 columns c0+8..c0+15 (of
+// the same token 16q + l).
+WR_DEVINL void acc_sum8(uint32_t taddr, int c0, bool upper, float (&o)[8]) {
+  uint32_t v[16];
+  tmem_ld16(taddr + c0, v);
+  tmem_wait_ld(v);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float x0 = __uint_as_float(v[c]), x1 = __uint_as_float(v[c + 8]);
+    const float s0 = x0 + __shfl_xor_sync(0xffffffffu, x0, 16);
+    const float s1 = x1 + __shfl_xor_sync(0xffffffffu, x1, 16);
+    o[c] = upper ? s1 : s0;
+  }
+}
+
+template <bool kGU>
+__global__ void __launch_bounds__(kGemmThreadsF, 1)
+    k_grouped_gemm_f32(const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ TokenMaps tm_b, const GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  griddep_launch_dependents();
+
+  // [token ring][fp32 landing ring][bf16 hi/lo ring][barriers]: a token slot
+  // holds 2n <= 128 rows; the MMA reads 128 (the overhang: stale rows of the
+  // next slot or the landing ring, feeding accumulator lanes nobody reads).
+  uint8_t* tring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* land = tring + kTStagesF * kTokBytes;
+  uint8_t* conv = land + kLStagesF * kLStageBytes;
+  uint64_t* fullL = reinterpret_cast<uint64_t*>(conv + kCStagesF * kCStageBytes);
+  uint64_t* emptyL = fullL + kLStagesF;
+  uint64_t* fullC = emptyL + kLStagesF;
+  uint64_t* emptyC = fullC + kCStagesF;
+  uint64_t* fullT = emptyC + kCStagesF;
+  uint64_t* emptyT = fullT + kTStagesF;
+  uint64_t* tfull = emptyT + kTStagesF;  // [2]
+  uint64_t* tempty = tfull + 2;          // [2]
+  uint64_t* drain = tempty + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLStagesF; ++s) {
+      mbar_init(&fullL[s], 1);
+      mbar_init(&emptyL[s], kConvWarps);
+    }
+    for (int s = 0; s < kCStagesF; ++s) {
+      mbar_init(&fullC[s], kConvWarps);
+      mbar_init(&emptyC[s], 1);
+    }
+    for (int s = 0; s < kTStagesF; ++s) {
+      mbar_init(&fullT[s], 1);
+      mbar_init(&emptyT[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_w);
+    for (int h = 0; h < kTokMaps; ++h) prefetch_tmap(&tm_b.m[h]);
+  }
+  griddep_wait();
+  {
+    WorkIter<kGU> probe;
+    if (!probe.init(a)) return;  // whole CTA: no work (uniform)
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemColsF);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const MetaView mv = meta_view(a.meta, a.E);
+
+  if (warp == 0 || warp == 6) {
+    // ---- TMA producers: warp 0 fp32 weights, warp 6 token tiles ----
+    if (lane == 0) {
+      const bool wprod = warp == 0;
+      const uint64_t pol = wprod ? l2_policy_evict_first() : l2_policy_evict_last();
+      uint64_t* full = wprod ? fullL : fullT;
+      uint64_t* empty = wprod ? emptyL : emptyT;
+      const int stages = wprod ? kLStagesF : kTStagesF;
+      uint8_t* ring = wprod ? land : tring;
+      const int sbytes = wprod ? kLStageBytes : kTokBytes;
+      int st = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      WorkIter<kGU> it;
+      it.init(a);
+      Work w;
+      while (ok && it.next(a, mv, w)) {
+        const int nbox = w.n / kBoxRows;  // <= 4: the 2n A rows are one box
+        for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+          const int kx = w.kc_at(i) * kBK;
+          if (!mbar_wait(&empty[st], ph ^ 1u, abort)) {
+            if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_EMPTY);
+            ok = false;
+            break;
+          }
+          uint8_t* s = ring + (size_t)st * sbytes;
+          if (wprod) {
+            // per K half: gate rows m0.. then up rows m0.. (64 each), or 128 rows of Wd
+            mbar_arrive_expect_tx(&full[st], (uint32_t)kLStageBytes);
+            for (int kh = 0; kh < 2; ++kh) {
+              uint8_t* d = s + kh * kLHalfBytes;
+              tma_load_3d(d, &tm_w, kx + 32 * kh, w.m0, w.e, &full[st], pol);
+              if (kGU)
+                tma_load_3d(d + kRowsAF * 128, &tm_w, kx + 32 * kh, a.I + w.m0, w.e, &full[st],
+                            pol);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full[st], (uint32_t)(2 * w.n * kRowB));
+            tma_load_2d(s, &tm_b.m[2 * nbox - 1], kx, 2 * w.row0, &full[st], pol);
+          }
+          ++issued;
+          if (++st == stages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      drain_ring(full, stages, issued, a.status);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      int sc = 0, stt = 0;
+      uint32_t phc = 0, pht = 0;
+      bool ok = true;
+      const uint32_t idesc = idesc_bf16(kTokM, kF32Rows);
+      WorkIter<kGU> it;
+      it.init(a);
+      Work w;
+      AccTurns acc;
+      acc.init();
+      while (ok && it.next(a, mv, w)) {
+        int b0, nb;
+        uint32_t aph[2];
+        acc.take(false, b0, nb, aph);
+        if (!mbar_wait(&tempty[b0], aph[0] ^ 1u, abort)) {
+          if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(b0 * kAccStrideF);
+        for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+          if (!mbar_wait(&fullC[sc], phc, abort) || !mbar_wait(&fullT[stt], pht, abort)) {
+            if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wh = smem_u32(conv + (size_t)sc * kCStageBytes);
+          const uint32_t ta = smem_u32(tring + (size_t)stt * kTokBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = sw128_desc(ta + kk * 32);
+            umma_bf16(d, ad, sw128_desc(wh + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(d, ad, sw128_desc(wh + kCHalfBytes + kk * 32), idesc, 1u);
+          }
+          umma_commit(&emptyC[sc]);
+          umma_commit(&emptyT[stt]);
+          if (++sc == kCStagesF) {
+            sc = 0;
+            phc ^= 1u;
+          }
+          if (++stt == kTStagesF) {
+            stt = 0;
+            pht ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b0]);
+      }
+      // Every MMA issued above must complete before TMEM is released.
+      umma_commit(drain);
+      if (!mbar_wait(drain, 0, nullptr)) atomicOr(a.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp >= 7) {
+    // ---- converters: fp32 landing stage -> bf16 hi and lo stages ----
+    // Warp cw converts rows cw, cw + 4, ..: lane l takes K elements 2l, 2l+1
+    // (landing half l / 16), so each row is one conflict-free 8-byte load per
+    // lane and one 4-byte store per lane into each of hi and lo.
+    const int cw = warp - 7;
+    const int kh = lane >> 4, kl = 2 * (lane & 15), k = 32 * kh + kl;
+    int sl = 0, sc = 0;
+    uint32_t phl = 0, phc = 0;
+    bool ok = true;
+    WorkIter<kGU> it;
+    it.init(a);
+    Work w;
+    while (ok && it.next(a, mv, w)) {
+      for (int i = 0; i < w.kc1 - w.kc0; ++i) {
+        const bool got =
+            mbar_wait(&fullL[sl], phl, abort) && mbar_wait(&emptyC[sc], phc ^ 1u, abort);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0 && !*abort) flag_timeout(a, abort, DEV_TIMEOUT_FULL);
+          ok = false;
+          break;
+        }
+        const uint8_t* L = land + (size_t)sl * kLStageBytes + kh * kLHalfBytes;
+        uint8_t* C = conv + (size_t)sc * kCStageBytes;
+        // rows r0 + 4j (j < kConvRows) per pass: all loads first, so they overlap
+        for (int r0 = cw; r0 < kF32Rows; r0 += kConvWarps * kConvRows) {
+          float2 v[kConvRows];
+#pragma unroll
+          for (int j = 0; j < kConvRows; ++j) {
+            const int r = r0 + kConvWarps * j;  // r & 7 == (r0 + 4j) & 7
+            v[j] = *reinterpret_cast<const float2*>(
+                L + r * 128 + ((((kl >> 2) ^ (r & 7)) << 4) | ((kl & 3) << 2)));
+          }
+#pragma unroll
+          for (int j = 0; j < kConvRows; ++j) {
+            const int r = r0 + kConvWarps * j;
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(v[j].x);
+            const __nv_bfloat16 h1 = __float2bfloat16_rn(v[j].y);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(v[j].x - __bfloat162float(h0));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(v[j].y - __bfloat162float(h1));
+            const int off = r * 128 + ((((k >> 3) ^ (r & 7)) << 4) | ((k & 7) << 1));
+            *reinterpret_cast<uint32_t*>(C + off) = pack_bf16x2(h0, h1);
+            *reinterpret_cast<uint32_t*>(C + kCHalfBytes + off) = pack_bf16x2(l0, l1);
+          }
+        }
+        fence_proxy_async_smem();  // the tensor core reads these stores
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&emptyL[sl]);
+          mbar_arrive(&fullC[sc]);
+        }
+        if (++sl == kLStagesF) {
+          sl = 0;
+          phl ^= 1u;
+        }
+        if (++sc == kCStagesF) {
+          sc = 0;
+          phc ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---- epilogue: warps 2..5, TMEM lane quarter warp % 4 ----
+    // Lane l < 16 of quarter q holds the hi part of token 16q + l, lane
+    // l + 16 its lo part: acc_sum8 adds them.
+    const int q = warp & 3;
+    const bool upper = lane >= 16;
+    const int half = upper ? 8 : 0;
+    WorkIter<kGU> it;
+    it.init(a);
+    Work w;
+    AccTurns acc;
+    acc.init();
+    while (it.next(a, mv, w)) {
+      int b0, nb;
+      uint32_t aph[2];
+      acc.take(false, b0, nb, aph);
+      bool bad = *abort != 0;
+      if (!bad && !mbar_wait(&tfull[b0], aph[0], abort)) {
+        if (!*abort) flag_timeout(a, abort, DEV_TIMEOUT_ACT);
+        bad = true;
+      }
+      if (named_bar_or(2, 128, bad)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b0 * kAccStrideF);
+      const int tok = 16 * q + (lane & 15);
+      const bool has = 16 * q < w.n;  // warp-uniform: this quarter holds tokens
+      const bool live = tok < w.n;
+      if (kGU) {
+        const bool whole = w.kc0 == 0 && w.kc1 == a.kc_total;
+        const int r = w.row0 + tok;
+        float* pb = a.pbuf +
+                    (((size_t)blockIdx.x * 2 + part_slot_of_piece(w)) * a.nmax + tok) * kF32Rows;
+        if (has) {
+          const float wt = live ? __ldg(a.row_w + r) : 0.0f;
+          uint16_t* hi = a.act + act_row_hi(r) * a.I;
+          uint16_t* lo = hi + 16 * (int64_t)a.I;
+          for (int c0 = 0; c0 < kRowsAF; c0 += 16) {
+            float g[8], u[8];
+            acc_sum8(taddr, c0, upper, g);
+            acc_sum8(taddr, kRowsAF + c0, upper, u);
+            if (!live) continue;
+            if (whole) {
+              swiglu_store8(g, u, wt, hi, lo, w.m0 + c0 + half, a.I);
+            } else {
+#pragma unroll
+              for (int k2 = 0; k2 < 2; ++k2) {
+                *reinterpret_cast<float4*>(pb + c0 + half + 4 * k2) =
+                    make_float4(g[4 * k2], g[4 * k2 + 1], g[4 * k2 + 2], g[4 * k2 + 3]);
+                *reinterpret_cast<float4*>(pb + kRowsAF + c0 + half + 4 * k2) =
+                    make_float4(u[4 * k2], u[4 * k2 + 1], u[4 * k2 + 2], u[4 * k2 + 3]);
+              }
+            }
+          }
+        }
+        release_acc(tempty, b0, 1, lane);
+        if (!whole) {
+          __threadfence();
+          named_bar_sync(1, 128);
+          const int cf = it.first_cta(w), cl = it.last_cta(a, w);
+          if (threadIdx.x == 64) {
+            const uint32_t done = atomicAdd(&a.cnt[w.tile], 1u);
+            *last_flag = done == (uint32_t)(cl - cf) ? 1 : 0;
+          }
+          named_bar_sync(1, 128);
+          if (*last_flag) {
+            __threadfence();
+            // item = (token, 16 rows of gate and of up); partials added in CTA order
+            const int et = threadIdx.x - 64;
+            for (int item = et; item < w.n * (kRowsAF / 16); item += 128) {
+              const int tt = item / (kRowsAF / 16);
+              const int c0 = (item % (kRowsAF / 16)) * 16;
+              const int rr = w.row0 + tt;
+              float4 gv[kJMaxA][4], uv[kJMaxA][4];
+#pragma unroll
+              for (int cc = 0; cc < kJMaxA; ++cc) {
+                if (cf + cc <= cl) {
+                  const float* src =
+                      a.pbuf +
+                      (((size_t)(cf + cc) * 2 + part_slot_of_cta(cf + cc, cf)) * a.nmax + tt) *
+                          kF32Rows;
+#pragma unroll
+                  for (int k4 = 0; k4 < 4; ++k4) {
+                    gv[cc][k4] = __ldcg(reinterpret_cast<const float4*>(src + c0) + k4);
+                    uv[cc][k4] = __ldcg(reinterpret_cast<const float4*>(src + kRowsAF + c0) + k4);
+                  }
+                }
+              }
+              float g[16], u[16];
+#pragma unroll
+              for (int c = 0; c < 16; ++c) g[c] = u[c] = 0.0f;
+#pragma unroll
+              for (int cc = 0; cc < kJMaxA; ++cc) {
+                if (cf + cc <= cl) {
+#pragma unroll
+                  for (int k4 = 0; k4 < 4; ++k4) {
+                    g[4 * k4] += gv[cc][k4].x; g[4 * k4 + 1] += gv[cc][k4].y;
+                    g[4 * k4 + 2] += gv[cc][k4].z; g[4 * k4 + 3] += gv[cc][k4].w;
+                    u[4 * k4] += uv[cc][k4].x; u[4 * k4 + 1] += uv[cc][k4].y;
+                    u[4 * k4 + 2] += uv[cc][k4].z; u[4 * k4 + 3] += uv[cc][k4].w;
+                  }
+                }
+              }
+              uint16_t* hrow = a.act + act_row_hi(rr) * a.I;
+              swiglu_store16(g, u, __ldg(a.row_w + rr), hrow, hrow + 16 * (int64_t)a.I,
+                             w.m0 + c0, a.I);
+            }
+            if (threadIdx.x == 64) a.cnt[w.tile] = 0;  // ready for the next call
+          }
+        }
+      } else {
+        if (has) {
+          float* yrow = a.ypart + ((int64_t)w.j * a.rmax + w.row0 + tok) * a.H;
+          for (int c0 = 0; c0 < kF32Rows; c0 += 16) {
+            float o[8];
+            acc_sum8(taddr, c0, upper, o);
+            const int h = w.m0 + c0 + half;
+            if (live) {
+#pragma unroll
+              for (int k2 = 0; k2 < 2; ++k2)
+                if (h + 4 * k2 < a.H)
+                  *reinterpret_cast<float4*>(yrow + h + 4 * k2) =
+                      make_float4(o[4 * k2], o[4 * k2 + 1], o[4 * k2 + 2], o[4 * k2 + 3]);
+            }
+          }
+        }
+        release_acc(tempty, b0, 1, lane);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemColsF);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -1422,12 +1905,13 @@ wr_status_t get_encoder(EncodeTiledFn* out) {
 
 // bf16 tensor map with 128-byte swizzling, zero fill outside the tensor.
 wr_status_t encode_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-                       const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+                       const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                       CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn enc;
   wr_status_t st = get_encoder(&enc);
   if (st != WR_OK) return st;
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
+  CUresult r = enc(m, dtype, (cuuint32_t)rank, const_cast<void*>(base),
                    dims, strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1457,6 +1941,8 @@ size_t a256(size_t n) { return (n + 255) & ~size_t(255); }
 
 // Everything the grouped path derives from the problem on the host.
 struct GroupedPlan {
+  bool f32;          // fp32 weights and tokens (k_grouped_gemm_f32)
+  int rowsA, rowsB;  // weight rows per tile (gate/up: of gate and of up; down: of Wd)
   int nmaxA, nmaxB;  // token rows per tile
   int rmax;          // row capacity (>= padded rows in use)
   int mtA, mtB;      // weight-row tiles per expert (gate/up over I, down over H)
@@ -1495,11 +1981,20 @@ GroupedPlan make_plan(const Problem& p) {
   GroupedPlan g;
   const int TK = p.T * p.K;
   const int n16 = (p.T + 15) & ~15;
-  g.nmaxA = n16 <= kNMaxA ? n16 : kNMaxAWide;
-  g.nmaxB = n16 <= kNMaxB ? n16 : kNMaxBWide;
+  g.f32 = p.dtype != WR_DTYPE_BF16;
+  if (g.f32) {
+    g.nmaxA = g.nmaxB = n16 < kNMaxF ? n16 : kNMaxF;
+    g.rowsA = kRowsAF;
+    g.rowsB = kRowsBF;
+  } else {
+    g.nmaxA = n16 <= kNMaxA ? n16 : kNMaxAWide;
+    g.nmaxB = n16 <= kNMaxB ? n16 : kNMaxBWide;
+    g.rowsA = kRowsA;
+    g.rowsB = kRowsB;
+  }
   g.rmax = (TK + 15 * p.ep_num + 15) & ~15;
-  g.mtA = (p.I + kRowsA - 1) / kRowsA;
-  g.mtB = (p.H + kRowsB - 1) / kRowsB;
+  g.mtA = (p.I + g.rowsA - 1) / g.rowsA;
+  g.mtB = (p.H + g.rowsB - 1) / g.rowsB;
   g.kcA = (p.H + kBK - 1) / kBK;
   g.kcB = (p.I + kBK - 1) / kBK;
   g.tbA = (g.nmaxA < kTokM ? g.nmaxA : kTokM) * kRowB;  // a wide tile takes two slots
@@ -1514,7 +2009,7 @@ GroupedPlan make_plan(const Problem& p) {
   g.off_rtok = o; o += a256(4 * (size_t)g.rmax);
   g.off_re = o; o += a256(16 * (size_t)g.rmax);
   g.off_rw = o; o += a256(4 * (size_t)g.rmax);
-  g.off_xg = o; o += a256(2 * (size_t)g.rmax * p.H);
+  g.off_xg = o; o += a256((g.f32 ? 4 : 2) * (size_t)g.rmax * p.H);  // fp32: hi and lo rows
   g.off_act = o; o += a256(2 * 2 * (size_t)g.rmax * p.I);
   // Down partials per tile: enough that the fewest possible tiles (one active
   // expert) still spread over every SM.
@@ -1522,7 +2017,8 @@ GroupedPlan make_plan(const Problem& p) {
   if (g.jmaxB < kJMaxB) g.jmaxB = kJMaxB;
   if (g.jmaxB > kJMaxBLimit) g.jmaxB = kJMaxBLimit;
   g.off_y = o; o += a256(4 * (size_t)g.jmaxB * g.rmax * p.H);
-  g.off_pbuf = o; o += a256(4 * (size_t)device_sm_count() * 2 * g.nmaxA * kWRows);
+  g.off_pbuf = o;
+  o += a256(4 * (size_t)device_sm_count() * 2 * g.nmaxA * (g.f32 ? kF32Rows : kWRows));
   g.cnt_words = g.mtA * (p.ep_num + (g.rmax + g.nmaxA - 1) / g.nmaxA);
   g.off_cnt = o; o += a256(4 * (size_t)g.cnt_words);
   g.total = o;
@@ -1548,15 +2044,17 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-template <bool kGU>
+template <bool kGU, bool kF32>
 wr_status_t set_smem_attr() {
   static std::once_flag once[64];
   static cudaError_t err[64];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    err[dev & 63] = cudaFuncSetAttribute(k_grouped_gemm<kGU>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+    err[dev & 63] = kF32 ? cudaFuncSetAttribute(k_grouped_gemm_f32<kGU>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemF)
+                         : cudaFuncSetAttribute(k_grouped_gemm<kGU>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
   });
   if (err[dev & 63] != cudaSuccess)
     return cuda_fail(err[dev & 63], "cudaFuncSetAttribute(grouped gemm)");
@@ -1566,8 +2064,8 @@ wr_status_t set_smem_attr() {
 }  // namespace
 
 bool grouped_supported(const Problem& p) {
-  return p.dtype == WR_DTYPE_BF16 && p.T >= kGroupedMinTokens && p.H % 8 == 0 && p.I % 8 == 0 &&
-         p.ep_num >= 1;
+  const int min_t = p.dtype == WR_DTYPE_BF16 ? kGroupedMinTokens : kGroupedMinTokensF32;
+  return p.T >= min_t && p.H % 8 == 0 && p.I % 8 == 0 && p.ep_num >= 1;
 }
 
 size_t grouped_workspace_bytes(const Problem& p) { return make_plan(p).total; }
@@ -1617,37 +2115,63 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   ba.cnt_words = g.cnt_words;
   const bool vec_ok = (reinterpret_cast<uintptr_t>(gate_w) & 15) == 0 &&
                       (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // H % 8 == 0 here
-  cudaError_t ce = launch_pdl(k_route_bucket, dim3(p.T), dim3(kRouteThreads), bucket_smem,
-                              stream, static_cast<const uint16_t*>(x),
-                              static_cast<const uint16_t*>(gate_w), p.router_bias, p.E, p.H,
-                              vec_ok, reinterpret_cast<uint32_t*>(ws), ids_d, w_d, ba);
+  cudaError_t ce =
+      g.f32 ? launch_pdl(k_route_bucket<float>, dim3(p.T), dim3(kRouteThreads), bucket_smem,
+                         stream, static_cast<const float*>(x), static_cast<const float*>(gate_w),
+                         p.router_bias, p.E, p.H, vec_ok, reinterpret_cast<uint32_t*>(ws), ids_d,
+                         w_d, ba)
+            : launch_pdl(k_route_bucket<uint16_t>, dim3(p.T), dim3(kRouteThreads), bucket_smem,
+                         stream, static_cast<const uint16_t*>(x),
+                         static_cast<const uint16_t*>(gate_w), p.router_bias, p.E, p.H, vec_ok,
+                         reinterpret_cast<uint32_t*>(ws), ids_d, w_d, ba);
   const int gather_blocks = g.rmax < 4 * sms ? g.rmax : 4 * sms;
   if (ce == cudaSuccess)
-    ce = launch_pdl(k_gather, dim3(gather_blocks), dim3(256), 0, stream,
-                    static_cast<const uint4*>(x), p.H / 8, (const int*)meta,
-                    (const int32_t*)rtok, reinterpret_cast<uint4*>(xg));
+    ce = g.f32 ? launch_pdl(k_gather_f32, dim3(gather_blocks), dim3(256), 0, stream,
+                            static_cast<const float4*>(x), p.H / 8, (const int*)meta,
+                            (const int32_t*)rtok, reinterpret_cast<uint4*>(xg))
+               : launch_pdl(k_gather, dim3(gather_blocks), dim3(256), 0, stream,
+                            static_cast<const uint4*>(x), p.H / 8, (const int*)meta,
+                            (const int32_t*)rtok, reinterpret_cast<uint4*>(xg));
   if (ce != cudaSuccess) return cuda_fail(ce, "bucket / gather launch");
 
-  const Layout lay = make_layout(p.H, p.I, 2);
+  const Layout lay = make_layout(p.H, p.I, g.f32 ? 4 : 2);
   const uint8_t* wb = static_cast<const uint8_t*>(wbuf);
   CUtensorMap tm_gu, tm_dn;
   TokenMaps tm_x, tm_act;
-  {
-    const cuuint64_t dims[3] = {(cuuint64_t)p.H, (cuuint64_t)2 * p.I, (cuuint64_t)p.ep_num};
-    const cuuint64_t str[2] = {(cuuint64_t)p.H * 2, (cuuint64_t)lay.stride};
-    const cuuint32_t box[3] = {kBK, kWBox, 1};
-    if ((st = encode_map(&tm_gu, wb + lay.off_gate, 3, dims, str, box)) != WR_OK) return st;
-  }
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)p.H, (cuuint64_t)g.rmax};
-    const cuuint64_t str[1] = {(cuuint64_t)p.H * 2};
-    if ((st = encode_token_maps(&tm_x, xg, dims, str, g.nmaxA, g.rmax)) != WR_OK) return st;
-  }
-  {
-    const cuuint64_t dims[3] = {(cuuint64_t)p.I, (cuuint64_t)p.H, (cuuint64_t)p.ep_num};
-    const cuuint64_t str[2] = {(cuuint64_t)p.I * 2, (cuuint64_t)lay.stride};
-    const cuuint32_t box[3] = {kBK, kWBox, 1};
-    if ((st = encode_map(&tm_dn, wb + lay.off_down, 3, dims, str, box)) != WR_OK) return st;
+  if (g.f32) {
+    // fp32 weights: per stage two K halves of 32 elements (128-byte rows);
+    // gate/up boxes of 64 rows (gate, then up), down boxes of 128 rows
+    constexpr CUtensorMapDataType f32t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const cuuint64_t dgu[3] = {(cuuint64_t)p.H, (cuuint64_t)2 * p.I, (cuuint64_t)p.ep_num};
+    const cuuint64_t sgu[2] = {(cuuint64_t)p.H * 4, (cuuint64_t)lay.stride};
+    const cuuint32_t bgu[3] = {32, kRowsAF, 1};
+    if ((st = encode_map(&tm_gu, wb + lay.off_gate, 3, dgu, sgu, bgu, f32t)) != WR_OK) return st;
+    const cuuint64_t ddn[3] = {(cuuint64_t)p.I, (cuuint64_t)p.H, (cuuint64_t)p.ep_num};
+    const cuuint64_t sdn[2] = {(cuuint64_t)p.I * 4, (cuuint64_t)lay.stride};
+    const cuuint32_t bdn[3] = {32, kRowsBF, 1};
+    if ((st = encode_map(&tm_dn, wb + lay.off_down, 3, ddn, sdn, bdn, f32t)) != WR_OK) return st;
+    // tokens: 2 rmax rows (hi / lo blocks of 16), boxes of up to 2 nmax rows
+    const cuuint64_t dx[2] = {(cuuint64_t)p.H, (cuuint64_t)2 * g.rmax};
+    const cuuint64_t sx[1] = {(cuuint64_t)p.H * 2};
+    if ((st = encode_token_maps(&tm_x, xg, dx, sx, 2 * g.nmaxA, 2 * g.rmax)) != WR_OK) return st;
+  } else {
+    {
+      const cuuint64_t dims[3] = {(cuuint64_t)p.H, (cuuint64_t)2 * p.I, (cuuint64_t)p.ep_num};
+      const cuuint64_t str[2] = {(cuuint64_t)p.H * 2, (cuuint64_t)lay.stride};
+      const cuuint32_t box[3] = {kBK, kWBox, 1};
+      if ((st = encode_map(&tm_gu, wb + lay.off_gate, 3, dims, str, box)) != WR_OK) return st;
+    }
+    {
+      const cuuint64_t dims[2] = {(cuuint64_t)p.H, (cuuint64_t)g.rmax};
+      const cuuint64_t str[1] = {(cuuint64_t)p.H * 2};
+      if ((st = encode_token_maps(&tm_x, xg, dims, str, g.nmaxA, g.rmax)) != WR_OK) return st;
+    }
+    {
+      const cuuint64_t dims[3] = {(cuuint64_t)p.I, (cuuint64_t)p.H, (cuuint64_t)p.ep_num};
+      const cuuint64_t str[2] = {(cuuint64_t)p.I * 2, (cuuint64_t)lay.stride};
+      const cuuint32_t box[3] = {kBK, kWBox, 1};
+      if ((st = encode_map(&tm_dn, wb + lay.off_down, 3, dims, str, box)) != WR_OK) return st;
+    }
   }
   {
     const cuuint64_t dims[2] = {(cuuint64_t)p.I, (cuuint64_t)2 * g.rmax};
@@ -1655,8 +2179,13 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
     if ((st = encode_token_maps(&tm_act, act, dims, str, 2 * g.nmaxB, 2 * g.rmax)) != WR_OK)
       return st;
   }
-  if ((st = set_smem_attr<true>()) != WR_OK) return st;
-  if ((st = set_smem_attr<false>()) != WR_OK) return st;
+  if (g.f32) {
+    if ((st = set_smem_attr<true, true>()) != WR_OK) return st;
+    if ((st = set_smem_attr<false, true>()) != WR_OK) return st;
+  } else {
+    if ((st = set_smem_attr<true, false>()) != WR_OK) return st;
+    if ((st = set_smem_attr<false, false>()) != WR_OK) return st;
+  }
 
   GemmArgs ga;
   ga.meta = meta;
@@ -1678,9 +2207,12 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   a1.wstages = g.wstA;
   a1.tstages = g.tstA;
   a1.tstage_bytes = g.tbA;
+  a1.mrows = g.rowsA;
   const size_t smemA = (size_t)g.wstA * kWStageBytes + (size_t)g.tstA * g.tbA + kSmemBase;
-  ce = launch_pdl(k_grouped_gemm<true>, dim3(sms), dim3(kGemmThreads), smemA, stream, tm_gu,
-                  tm_x, a1);
+  ce = g.f32 ? launch_pdl(k_grouped_gemm_f32<true>, dim3(sms), dim3(kGemmThreadsF),
+                          (size_t)kSmemF, stream, tm_gu, tm_x, a1)
+             : launch_pdl(k_grouped_gemm<true>, dim3(sms), dim3(kGemmThreads), smemA, stream,
+                          tm_gu, tm_x, a1);
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (gate/up) launch");
 
   GemmArgs a2 = ga;
@@ -1690,10 +2222,13 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   a2.wstages = g.wstB;
   a2.tstages = g.tstB;
   a2.tstage_bytes = g.tbB;
+  a2.mrows = g.rowsB;
   const size_t smemB = (size_t)g.wstB * kWStageBytes + (size_t)g.tstB * g.tbB +
                        kSmemBase;
-  ce = launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream, tm_dn,
-                  tm_act, a2);
+  ce = g.f32 ? launch_pdl(k_grouped_gemm_f32<false>, dim3(sms), dim3(kGemmThreadsF),
+                          (size_t)kSmemF, stream, tm_dn, tm_act, a2)
+             : launch_pdl(k_grouped_gemm<false>, dim3(sms), dim3(kGemmThreads), smemB, stream,
+                          tm_dn, tm_act, a2);
   if (ce != cudaSuccess) return cuda_fail(ce, "grouped GEMM (down) launch");
 
   const int H4 = p.H / 4;
@@ -1705,8 +2240,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
       if (blocks > 4 * sms) blocks = 4 * sms;
       ce = launch_pdl(k_combine_ar, dim3(blocks), dim3(256), 0, stream,
                       reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                      (const int4*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, sms,
-                      g.jmaxB, t0, Tc, *comm, p.res,
+                      (const int4*)rtile, (const int*)meta, p.K, p.H, g.rmax, g.kcB, g.rowsB,
+                      sms, g.jmaxB, t0, Tc, *comm, p.res,
                       reinterpret_cast<uint32_t*>(ws), out);
       if (ce != cudaSuccess) return cuda_fail(ce, "combine (all-reduce) launch");
     }
@@ -1714,8 +2249,8 @@ wr_status_t launch_grouped(const Problem& p, const void* x, const void* gate_w, 
   }
   ce = launch_pdl(k_combine, dim3(p.T, (H4 + 255) / 256), dim3(256), 0, stream,
                   reinterpret_cast<const float4*>(ypart), (const int32_t*)slot,
-                  (const int4*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, sms, g.jmaxB,
-                  p.res, reinterpret_cast<float4*>(out));
+                  (const int4*)rtile, (const int*)meta, p.K, H4, g.rmax, g.kcB, g.rowsB, sms,
+                  g.jmaxB, p.res, reinterpret_cast<float4*>(out));
   return ce == cudaSuccess ? WR_OK : cuda_fail(ce, "combine launch");
 }
 

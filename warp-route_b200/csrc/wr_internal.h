@@ -75,7 +75,8 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
 // ---- grouped tensor-core path for token batches (wr_grouped.cu) ----
 // Batches of at least this many bf16 tokens run as grouped GEMMs over
 // tokens bucketed per expert (a single token takes the streaming kernel).
-constexpr int kGroupedMinTokens = 2;
+constexpr int kGroupedMinTokens = 2;     // bf16 batches from 2 tokens run as grouped GEMMs
+constexpr int kGroupedMinTokensF32 = 5;  // fp32: up to 4 tokens stream in one pass
 bool grouped_supported(const Problem& p);
 size_t grouped_workspace_bytes(const Problem& p);
 // comm: null, or the communicator whose ranks' partial outputs the combine
