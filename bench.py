@@ -35,6 +35,10 @@ layer calls.  Batches of two or more bf16 tokens run on the grouped
 tensor-core path (tcgen05 GEMMs over tokens bucketed per expert).  At N > 1
 the sweep is expert parallel (E/N experts of every layer per GPU) with one
 NCCL all-reduce of the layer output, both inside the replayed graph.
+`batched_sweep_fp32` is the same sweep in fp32, warp-route's own dtype
+(tokens 16 and 64, 8 stacked layers of 5.6 GB): batches of five or more fp32
+tokens take the grouped path with the weights split into bf16 hi and lo
+parts in shared memory.
 """
 from __future__ import annotations
 
@@ -84,6 +88,9 @@ def parse():
     ap.add_argument("--sweep-tokens", default="1,4,16,64,256",
                     help="batched-decode sweep token counts; empty: no sweep")
     ap.add_argument("--sweep-layers", type=int, default=32)
+    ap.add_argument("--fp32-sweep-tokens", default="16,64",
+                    help="the same sweep in fp32 (warp-route's dtype); empty: none")
+    ap.add_argument("--fp32-sweep-layers", type=int, default=8)
     ap.add_argument("--sweep-steps", type=int, default=3)
     ap.add_argument("--sweep-fused-allreduce", action="store_true",
                     help="N > 1: sum the sweep's batch outputs in the layer's combine step "
@@ -314,7 +321,7 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def batched_sweep(args, dev, world=1, rank=0, comm=None):
+def batched_sweep(args, dev, world=1, rank=0, comm=None, dtype=torch.bfloat16):
     """The batched-decode sweep (Mixtral shape, router bias, stacked layers):
     per token count, µs per layer over CUDA-graph replays of one step (every
     layer once) and the HBM GB/s of the distinct experts each layer streams.
@@ -327,14 +334,17 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
     from warp_route import functional as F
     from warp_route import synthetic
 
-    tokens = [int(t) for t in args.sweep_tokens.split(",") if t.strip()]
+    f32 = dtype == torch.float32
+    spec = args.fp32_sweep_tokens if f32 else args.sweep_tokens
+    tokens = [int(t) for t in spec.split(",") if t.strip()]
     if not tokens:
         return None
     E, H, I, K = SHAPES["mixtral"]
     if E % world:
         return None
-    nl = args.sweep_layers
-    layers = [synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, device=dev, seed=900 + li,
+    nl = args.fp32_sweep_layers if f32 else args.sweep_layers
+    elt = 4 if f32 else 2
+    layers = [synthetic.make_layer(E, H, I, K, dtype=dtype, device=dev, seed=900 + li,
                                    layer=li, router_bias=True, ep_rank=rank, ep_size=world)
               for li in range(nl)]
     results = []
@@ -343,7 +353,7 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
     for T in tokens:
         gx = torch.Generator(device=dev)
         gx.manual_seed(7000 + T)
-        x = torch.randn(T, H, generator=gx, device=dev).to(torch.bfloat16)
+        x = torch.randn(T, H, generator=gx, device=dev).to(dtype)
         xin = x[0].contiguous() if T == 1 else x
         distinct, local_max = [], []
         for Lr in layers:
@@ -401,14 +411,16 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
         del g
         torch.cuda.synchronize()
         mean_distinct = sum(distinct) / len(distinct)
-        wbytes = mean_distinct * 3 * H * I * 2
+        wbytes = mean_distinct * 3 * H * I * elt
         gbs = wbytes / (us * 1e-6) / 1e9
         peak, _ = peaks()
         r = {"tokens": T, "us_per_layer": round(us, 2),
              "hbm_gbs": round(gbs, 1),
              "frac_of_hbm_peak": round(gbs / (peak * world), 4),
              "experts_per_layer": round(mean_distinct, 2),
-             "path": "streaming kernel" if T == 1 else "grouped tcgen05 GEMMs",
+             "path": ("streaming kernel" if T == 1 or (f32 and T < 5) else
+                      "grouped tcgen05 GEMMs, fp32 split into bf16 hi + lo" if f32 else
+                      "grouped tcgen05 GEMMs"),
              "clocks": clk.summary()}
         if world > 1:
             r["busiest_rank_experts"] = round(sum(local_max) / len(local_max), 2)
@@ -420,7 +432,7 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None):
            else "NCCL all-reduce")
     par = (f"expert parallel over {world} GPUs ({E // world} experts each), [T,H] fp32 output "
            f"{how}, in the graph" if world > 1 else "single GPU")
-    return {"config": "mixtral, router bias N(0,1), bf16", "layers": nl,
+    return {"config": f"mixtral, router bias N(0,1), {'fp32' if f32 else 'bf16'}", "layers": nl,
             "steps": args.sweep_steps, "parallelism": par,
             "note": "each layer has its own weights, gate and bias and takes the same seeded "
                     "token batch; value = µs per layer (graph replays of the layer stack, max "
@@ -936,6 +948,9 @@ def run_ours(args, world, rank, local):
             torch.cuda.synchronize()
             dist.barrier()
             comm.close()
+    sweep32 = None
+    if args.fp32_sweep_tokens.strip():
+        sweep32 = batched_sweep(args, dev, world, rank, None, dtype=torch.float32)
 
     dec = decode_step(args, dev, world, rank)
 
@@ -956,6 +971,8 @@ def run_ours(args, world, rank, local):
             line["other_configs"] = extras
         if sweep is not None:
             line["batched_sweep"] = sweep
+        if sweep32 is not None:
+            line["batched_sweep_fp32"] = sweep32
         if dec is not None:
             line["decode_step"] = dec
         print(json.dumps(line), flush=True)
@@ -974,8 +991,11 @@ def main():
         if world != 1:
             raise SystemExit("--only-sweep runs on one GPU")
         torch.cuda.set_device(local)
-        sweep = batched_sweep(args, torch.device("cuda", local))
-        print(json.dumps({"batched_sweep": sweep}), flush=True)
+        dev = torch.device("cuda", local)
+        out = {"batched_sweep": batched_sweep(args, dev)}
+        if args.fp32_sweep_tokens.strip():
+            out["batched_sweep_fp32"] = batched_sweep(args, dev, dtype=torch.float32)
+        print(json.dumps(out), flush=True)
         return
     run_ours(args, world, rank, local)
 

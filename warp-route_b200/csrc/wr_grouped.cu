@@ -1462,7 +1462,7 @@ constexpr int kCHalfBytes = kF32Rows * kRowB;     // 16 KB: 128 bf16 rows of 64 
 constexpr int kCStageBytes = 2 * kCHalfBytes;     // hi rows, then lo rows
 constexpr int kLStagesF = 4, kCStagesF = 2, kTStagesF = 2;
 constexpr int kConvWarps = 4;                     // warps 7..10
-constexpr int kConvRows = 8;                      // rows a converter lane has in flight
+constexpr int kConvRows = 4;                      // rows a converter lane has in flight
 constexpr int kGemmThreadsF = 32 * (7 + kConvWarps);
 constexpr int kTmemColsF = 256;                   // two accumulators of 128 columns
 constexpr int kAccStrideF = 128;
@@ -1681,11 +1681,14 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
     }
   } else if (warp >= 7) {
     // ---- converters: fp32 landing stage -> bf16 hi and lo stages ----
-    // Warp cw converts rows cw, cw + 4, ..: lane l takes K elements 2l, 2l+1
-    // (landing half l / 16), so each row is one conflict-free 8-byte load per
-    // lane and one 4-byte store per lane into each of hi and lo.
+    // Lane l takes K elements 4c..4c+3 (c = l % 16: one 16-byte chunk of
+    // the landing row, half c / 8) of row 2p + l / 16 of each row pair p the
+    // warp converts (pairs cw, cw + 4, ..): one 16-byte load, two packed
+    // conversions per part, one 8-byte store into each of hi and lo; each
+    // 8-lane group reads and writes whole 128-byte rows (no bank conflicts).
     const int cw = warp - 7;
-    const int kh = lane >> 4, kl = 2 * (lane & 15), k = 32 * kh + kl;
+    const int c = lane & 15, rp = lane >> 4;
+    const int lhalf = (c >> 3) * kLHalfBytes;
     int sl = 0, sc = 0;
     uint32_t phl = 0, phc = 0;
     bool ok = true;
@@ -1701,27 +1704,32 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
           ok = false;
           break;
         }
-        const uint8_t* L = land + (size_t)sl * kLStageBytes + kh * kLHalfBytes;
+        const uint8_t* L = land + (size_t)sl * kLStageBytes + lhalf;
         uint8_t* C = conv + (size_t)sc * kCStageBytes;
-        // rows r0 + 4j (j < kConvRows) per pass: all loads first, so they overlap
-        for (int r0 = cw; r0 < kF32Rows; r0 += kConvWarps * kConvRows) {
-          float2 v[kConvRows];
+        // kConvRows rows in flight per lane: all loads first, so they overlap
+        for (int p0 = cw; p0 < kF32Rows / 2; p0 += kConvWarps * kConvRows) {
+          float4 v[kConvRows];
 #pragma unroll
           for (int j = 0; j < kConvRows; ++j) {
-            const int r = r0 + kConvWarps * j;  // r & 7 == (r0 + 4j) & 7
-            v[j] = *reinterpret_cast<const float2*>(
-                L + r * 128 + ((((kl >> 2) ^ (r & 7)) << 4) | ((kl & 3) << 2)));
+            const int r = 2 * (p0 + kConvWarps * j) + rp;
+            v[j] = *reinterpret_cast<const float4*>(L + r * 128 + (((c & 7) ^ (r & 7)) << 4));
           }
 #pragma unroll
           for (int j = 0; j < kConvRows; ++j) {
-            const int r = r0 + kConvWarps * j;
-            const __nv_bfloat16 h0 = __float2bfloat16_rn(v[j].x);
-            const __nv_bfloat16 h1 = __float2bfloat16_rn(v[j].y);
-            const __nv_bfloat16 l0 = __float2bfloat16_rn(v[j].x - __bfloat162float(h0));
-            const __nv_bfloat16 l1 = __float2bfloat16_rn(v[j].y - __bfloat162float(h1));
-            const int off = r * 128 + ((((k >> 3) ^ (r & 7)) << 4) | ((k & 7) << 1));
-            *reinterpret_cast<uint32_t*>(C + off) = pack_bf16x2(h0, h1);
-            *reinterpret_cast<uint32_t*>(C + kCHalfBytes + off) = pack_bf16x2(l0, l1);
+            const int r = 2 * (p0 + kConvWarps * j) + rp;
+            const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[j].x, v[j].y);
+            const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[j].z, v[j].w);
+            const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[j].x - __low2float(h01),
+                                                             v[j].y - __high2float(h01));
+            const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[j].z - __low2float(h23),
+                                                             v[j].w - __high2float(h23));
+            const int off = r * 128 + ((((c >> 1) ^ (r & 7)) << 4) | ((c & 1) << 3));
+            *reinterpret_cast<uint2*>(C + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                           *reinterpret_cast<const uint32_t*>(&h23));
+            *reinterpret_cast<uint2*>(C + kCHalfBytes + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&l01),
+                           *reinterpret_cast<const uint32_t*>(&l23));
           }
         }
         fence_proxy_async_smem();  // the tensor core reads these stores
