@@ -1686,9 +1686,16 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
     // warp converts (pairs cw, cw + 4, ..): one 16-byte load, two packed
     // conversions per part, one 8-byte store into each of hi and lo; each
     // 8-lane group reads and writes whole 128-byte rows (no bank conflicts).
+    // A lane's rows r = 2 (cw + 4 j) + l / 16 all have the same r % 8, so its
+    // swizzled chunk positions are fixed and the rows 1 KB apart.
     const int cw = warp - 7;
     const int c = lane & 15, rp = lane >> 4;
-    const int lhalf = (c >> 3) * kLHalfBytes;
+    const int sw = (2 * cw + rp) & 7;
+    const int row0 = (2 * cw + rp) * 128;
+    const int ld_off = (c >> 3) * kLHalfBytes + row0 + (((c & 7) ^ sw) << 4);
+    const int st_off = row0 + ((((c >> 1) ^ sw) << 4) | ((c & 1) << 3));
+    constexpr int kRowStep = 2 * kConvWarps * 128;  // bytes between a lane's rows
+    constexpr int kLaneRows = kF32Rows / (2 * kConvWarps);
     int sl = 0, sc = 0;
     uint32_t phl = 0, phc = 0;
     bool ok = true;
@@ -1704,30 +1711,27 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
           ok = false;
           break;
         }
-        const uint8_t* L = land + (size_t)sl * kLStageBytes + lhalf;
-        uint8_t* C = conv + (size_t)sc * kCStageBytes;
+        const uint8_t* L = land + (size_t)sl * kLStageBytes + ld_off;
+        uint8_t* C = conv + (size_t)sc * kCStageBytes + st_off;
         // kConvRows rows in flight per lane: all loads first, so they overlap
-        for (int p0 = cw; p0 < kF32Rows / 2; p0 += kConvWarps * kConvRows) {
+#pragma unroll
+        for (int j0 = 0; j0 < kLaneRows; j0 += kConvRows) {
           float4 v[kConvRows];
 #pragma unroll
-          for (int j = 0; j < kConvRows; ++j) {
-            const int r = 2 * (p0 + kConvWarps * j) + rp;
-            v[j] = *reinterpret_cast<const float4*>(L + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-          }
+          for (int j = 0; j < kConvRows; ++j)
+            v[j] = *reinterpret_cast<const float4*>(L + (j0 + j) * kRowStep);
 #pragma unroll
           for (int j = 0; j < kConvRows; ++j) {
-            const int r = 2 * (p0 + kConvWarps * j) + rp;
             const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[j].x, v[j].y);
             const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[j].z, v[j].w);
             const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[j].x - __low2float(h01),
                                                              v[j].y - __high2float(h01));
             const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[j].z - __low2float(h23),
                                                              v[j].w - __high2float(h23));
-            const int off = r * 128 + ((((c >> 1) ^ (r & 7)) << 4) | ((c & 1) << 3));
-            *reinterpret_cast<uint2*>(C + off) =
-                make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
-                           *reinterpret_cast<const uint32_t*>(&h23));
-            *reinterpret_cast<uint2*>(C + kCHalfBytes + off) =
+            uint8_t* d = C + (j0 + j) * kRowStep;
+            *reinterpret_cast<uint2*>(d) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                                                      *reinterpret_cast<const uint32_t*>(&h23));
+            *reinterpret_cast<uint2*>(d + kCHalfBytes) =
                 make_uint2(*reinterpret_cast<const uint32_t*>(&l01),
                            *reinterpret_cast<const uint32_t*>(&l23));
           }
