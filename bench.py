@@ -36,7 +36,7 @@ tensor-core path (tcgen05 GEMMs over tokens bucketed per expert).  At N > 1
 the sweep is expert parallel (E/N experts of every layer per GPU) with one
 NCCL all-reduce of the layer output, both inside the replayed graph.
 `batched_sweep_fp32` is the same sweep in fp32, warp-route's own dtype
-(tokens 16 and 64, 8 stacked layers of 5.6 GB): batches of five or more fp32
+(tokens 16 and 64, 8 stacked layers of 5.6 GB): batches of three or more fp32
 tokens take the grouped path with the weights split into bf16 hi and lo
 parts in shared memory.
 """
@@ -418,7 +418,7 @@ def batched_sweep(args, dev, world=1, rank=0, comm=None, dtype=torch.bfloat16):
              "hbm_gbs": round(gbs, 1),
              "frac_of_hbm_peak": round(gbs / (peak * world), 4),
              "experts_per_layer": round(mean_distinct, 2),
-             "path": ("streaming kernel" if T == 1 or (f32 and T < 5) else
+             "path": ("streaming kernel" if T == 1 or (f32 and T < 3) else
                       "grouped tcgen05 GEMMs, fp32 split into bf16 hi + lo" if f32 else
                       "grouped tcgen05 GEMMs"),
              "clocks": clk.summary()}

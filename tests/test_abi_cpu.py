@@ -138,12 +138,11 @@ def test_grouped_workspace_covers_its_buffers():
     assert need >= rows * H * 2 + 2 * rows * I * 2 + 4 * rows * H * 4
     # one token keeps the streaming kernel's much smaller workspace
     assert lib.wr_fused_moe_workspace_size(ctypes.byref(d), 1) < rows * I * 2
-    # fp32 batches of 5 or more tokens take the fp32 grouped path: the tokens
-    # bucketed as bf16 hi and lo rows; up to 4 tokens stay on the streaming
-    # kernel
+    # fp32 batches of 3 or more tokens take the fp32 grouped path: the tokens
+    # bucketed as bf16 hi and lo rows; 2 tokens stay on the streaming kernel
     d32 = _abi.desc(E, H, I, K, _abi.WR_DTYPE_F32)
     assert lib.wr_fused_moe_workspace_size(ctypes.byref(d32), T) >= 2 * rows * H * 2
-    assert lib.wr_fused_moe_workspace_size(ctypes.byref(d32), 4) < rows * I * 2
+    assert lib.wr_fused_moe_workspace_size(ctypes.byref(d32), 2) < rows * I * 2
     # grows with the batch
     assert lib.wr_fused_moe_workspace_size(ctypes.byref(d), 2 * T) > need
 

@@ -214,7 +214,7 @@ def test_deterministic_and_workspace_reusable():
     (4, 1024, 1536, 4, 64),    # top_k 4: experts with up to 64 tokens, one tile each
     (8, 1024, 2048, 2, 130),   # experts with several 64-token tiles
     (64, 256, 128, 8, 40),     # the most experts, top_k 8: many small buckets
-    (8, 512, 1024, 2, 5),      # the smallest fp32 batch on the grouped path
+    (8, 512, 1024, 2, 3),      # the smallest fp32 batch on the grouped path
 ])
 def test_fp32_batches_grouped(E, H, I, K, T):
     """fp32 batches (warp-route's dtype) on the tensor cores: weights split

@@ -107,9 +107,10 @@ wr_status_t check_ws(void* ws, size_t have, size_t need) {
 }
 
 size_t fused_ws_for(const Problem& p) {
-  // Batches of kGroupedMinTokens or more bf16 tokens run as grouped GEMMs;
-  // otherwise the batched entry point runs blocks of up to 4 tokens through
-  // the streaming kernel, and unsupported shapes go through the naive path.
+  // Batches of kGroupedMinTokens or more bf16 tokens (kGroupedMinTokensF32
+  // fp32 tokens) run as grouped GEMMs; otherwise the batched entry point runs
+  // blocks of up to 4 tokens through the streaming kernel, and unsupported
+  // shapes go through the naive path.
   Problem q = p;
   q.T = p.T < 1 ? 1 : (p.T > 4 ? 4 : p.T);
   size_t need = naive_workspace_bytes(p);

@@ -1,5 +1,5 @@
-// wr_grouped.cu — the batched layer (two or more bf16 tokens) as two grouped
-// GEMMs on the 5th-generation tensor cores.
+// wr_grouped.cu — the batched layer (two or more bf16 tokens, three or more
+// fp32 tokens) as two grouped GEMMs on the 5th-generation tensor cores.
 //
 // warp-route's batched kernel (src/fused_moe_batched.cu:20-183) gives every
 // token its own CTA and streams every selected expert's weights once per
@@ -14,8 +14,9 @@
 //                   of 16 rows with zero-weight rows
 //   k_gather        X_g[row] = x[token of row] (bf16), zero for padding
 //   k_grouped_gemm<gate/up>
-//                   tile = (expert, 128 intermediate rows, <= 128 tokens):
-//                   D[token, 256] = X_g rows x [128 gate rows; 128 up rows],
+//                   tile = (expert, 128 intermediate rows, <= 256 tokens):
+//                   D[token, 256] = X_g rows x [128 gate rows; 128 up rows]
+//                   (tokens 128.. of a tile in the second accumulator),
 //                   epilogue act = silu(g) * u * w(token, k) stored as bf16
 //                   hi + lo (~16 mantissa bits for the second GEMM), in
 //                   blocks of 16 act_hi rows each followed by their act_lo
@@ -41,8 +42,13 @@
 // epilogue); warps 2-5 read the accumulators back with tcgen05.ld (warp w
 // reads TMEM lanes 32*(w%4)..+31) and store the results.  Two accumulator
 // buffers let the epilogue of one tile overlap the MMAs of the next (down
-// tiles above 64 tokens use both).  The K chunks of all tiles are dealt to
-// the CTAs in equal ranges (stream-K; the down GEMM's weighted by cost).
+// tiles above 64 tokens and gate/up tiles above 128 use both).  The K
+// chunks of all tiles are dealt to the CTAs in ranges of equal cost
+// (stream-K; a chunk of a tile that uses both accumulators costs more).
+//
+// fp32 (warp-route's dtype): k_gather_f32 and k_grouped_gemm_f32, the same
+// structure with every fp32 operand split into bf16 hi + lo (weights by
+// converter warps in shared memory); see k_grouped_gemm_f32.
 // No TMA multicast anywhere; every wait is bounded and a wait that runs out
 // sets the workspace status word and winds the CTA down (copies in flight
 // drained, MMAs completed, TMEM freed).

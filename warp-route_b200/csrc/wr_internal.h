@@ -73,10 +73,10 @@ wr_status_t launch_fused(const Problem& p, const void* x, const void* gate_w,
                          void* ws, cudaStream_t stream, const CommView* comm = nullptr);
 
 // ---- grouped tensor-core path for token batches (wr_grouped.cu) ----
-// Batches of at least this many bf16 tokens run as grouped GEMMs over
-// tokens bucketed per expert (a single token takes the streaming kernel).
+// Batches of at least this many tokens run as grouped GEMMs over tokens
+// bucketed per expert (fewer take the streaming kernel).
 constexpr int kGroupedMinTokens = 2;     // bf16 batches from 2 tokens run as grouped GEMMs
-constexpr int kGroupedMinTokensF32 = 5;  // fp32: up to 4 tokens stream in one pass
+constexpr int kGroupedMinTokensF32 = 3;  // fp32: 2 tokens stream faster (measured)
 bool grouped_supported(const Problem& p);
 size_t grouped_workspace_bytes(const Problem& p);
 // comm: null, or the communicator whose ranks' partial outputs the combine
