@@ -1444,19 +1444,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // ---------------------------------------------------------------------------
 // fp32 weights (warp-route's own dtype) on the same tensor cores.  The MMAs
-// take bf16 operands, so every fp32 value v is split into hi = rn(v) and
-// lo = rn(v - hi) (together exact to about 2^-17 relative):
-//   * tokens and activations: hi and lo rows interleaved in blocks of 16
-//     (act_row_hi), so one MMA's 128 A rows hold 64 tokens' hi and lo parts
-//     in accumulator lanes 32q + l and 32q + 16 + l, added by one shuffle;
+// take bf16 operands, so every fp32 value is split into two bf16 parts:
+//   * tokens and activations: hi = rn(v), lo = rn(v - hi) (about 2^-17
+//     relative), hi and lo rows interleaved in blocks of 16 (act_row_hi), so
+//     one MMA's 128 A rows hold 64 tokens' hi and lo parts in accumulator
+//     lanes 32q + l and 32q + 16 + l, added by one shuffle;
 //   * weights: the fp32 rows land in shared memory by TMA (two 128-byte
 //     swizzled boxes of 32 K elements per stage) and four converter warps
-//     write their hi and lo parts as two bf16 stages in the MMA layout.
-// Per K step of 16: D += A x W_hi, D += A x W_lo (N = 128 weight rows), so D
-// holds (x_hi + x_lo) . (w_hi + w_lo) summed in fp32.  Tiles: gate/up 64
-// gate + 64 up rows (accumulator columns 0..63 / 64..127), down 128 rows of
-// Wd; at most 64 tokens per tile.  The weights stream from HBM once per
-// batch; each byte of them is read by the TMA and once more by a converter.
+//     write hi = the upper 16 bits of v and lo = the upper 16 bits of the
+//     exact remainder v - hi (bit operations only; |v - hi - lo| < 2^-14 |v|)
+//     as 128 hi rows followed by 128 lo rows in the MMA layout.
+// Per K step of 16 one MMA with N = 256: B = [W_hi; W_lo], so accumulator
+// columns c and 128 + c hold A.w_hi and A.w_lo of weight row c, added in
+// the epilogue; the sum is (x_hi + x_lo) . (w_hi + w_lo) in fp32.  Tiles:
+// gate/up 64 gate + 64 up rows (columns 0..63 / 64..127 of each half), down
+// 128 rows of Wd; at most 64 tokens per tile.  The weights stream from HBM
+// once per batch; each byte of them is read by the TMA and once more by a
+// converter.  Shared-memory traffic (TMA writes, the converters' reads and
+// writes, the MMA's operand reads) is about 160 KB per 32 KB weight stage.
 // ---------------------------------------------------------------------------
 constexpr int kF32Rows = 128;                     // weight rows per stage and MMA N
 constexpr int kRowsAF = 64;                       // gate/up tile: rows of gate and of up
@@ -1470,8 +1475,8 @@ constexpr int kLStagesF = 4, kCStagesF = 2, kTStagesF = 2;
 constexpr int kConvWarps = 4;                     // warps 7..10
 constexpr int kConvRows = 4;                      // rows a converter lane has in flight
 constexpr int kGemmThreadsF = 32 * (7 + kConvWarps);
-constexpr int kTmemColsF = 256;                   // two accumulators of 128 columns
-constexpr int kAccStrideF = 128;
+constexpr int kTmemColsF = 512;                   // two accumulators of 256 columns
+constexpr int kAccStrideF = 256;
 constexpr int kSmemF = kTStagesF * kTokBytes + kLStagesF * kLStageBytes +
                        kCStagesF * kCStageBytes + kSmemBase;
 static_assert(kSmemF <= kSmemMax, "fp32 grouped GEMM shared memory");
@@ -1498,16 +1503,20 @@ WR_DEVINL void swiglu_store8(const float (&g)[8], const float (&u)[8], float wt,
   *reinterpret_cast<uint4*>(lo + i) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
 }
 
-// The 16 columns c0.. of this lane's accumulator row, hi and lo lanes added:
-// lanes l < 16 get columns c0..c0+7, lanes l + 16 columns c0+8..c0+15 (of
-// the same token 16q + l).
+// Weight rows c0..c0+15 of this lane's accumulator row: the W_hi column
+// c plus the W_lo column 128 + c, hi and lo token lanes added: lanes l < 16
+// get rows c0..c0+7, lanes l + 16 rows c0+8..c0+15 (of the same token
+// 16q + l).
 WR_DEVINL void acc_sum8(uint32_t taddr, int c0, bool upper, float (&o)[8]) {
-  uint32_t v[16];
+  uint32_t v[16], u[16];
   tmem_ld16(taddr + c0, v);
+  tmem_ld16(taddr + kF32Rows + c0, u);
   tmem_wait_ld(v);
+  reg_dep16(u);
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    const float x0 = __uint_as_float(v[c]), x1 = __uint_as_float(v[c + 8]);
+    const float x0 = __uint_as_float(v[c]) + __uint_as_float(u[c]);
+    const float x1 = __uint_as_float(v[c + 8]) + __uint_as_float(u[c + 8]);
     const float s0 = x0 + __shfl_xor_sync(0xffffffffu, x0, 16);
     const float s1 = x1 + __shfl_xor_sync(0xffffffffu, x1, 16);
     o[c] = upper ? s1 : s0;
@@ -1636,7 +1645,7 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
       int sc = 0, stt = 0;
       uint32_t phc = 0, pht = 0;
       bool ok = true;
-      const uint32_t idesc = idesc_bf16(kTokM, kF32Rows);
+      const uint32_t idesc = idesc_bf16(kTokM, 2 * kF32Rows);  // B = [W_hi; W_lo]
       WorkIter<kGU> it;
       it.init(a);
       Work w;
@@ -1663,9 +1672,8 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
           const uint32_t ta = smem_u32(tring + (size_t)stt * kTokBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = sw128_desc(ta + kk * 32);
-            umma_bf16(d, ad, sw128_desc(wh + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
-            umma_bf16(d, ad, sw128_desc(wh + kCHalfBytes + kk * 32), idesc, 1u);
+            umma_bf16(d, sw128_desc(ta + kk * 32), sw128_desc(wh + kk * 32), idesc,
+                      (i > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&emptyC[sc]);
           umma_commit(&emptyT[stt]);
@@ -1689,8 +1697,9 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
     // ---- converters: fp32 landing stage -> bf16 hi and lo stages ----
     // Lane l takes K elements 4c..4c+3 (c = l % 16: one 16-byte chunk of
     // the landing row, half c / 8) of row 2p + l / 16 of each row pair p the
-    // warp converts (pairs cw, cw + 4, ..): one 16-byte load, two packed
-    // conversions per part, one 8-byte store into each of hi and lo; each
+    // warp converts (pairs cw, cw + 4, ..): one 16-byte load, the hi parts
+    // (upper halves) and the exact remainders by bit masks and subtractions,
+    // byte permutes to pack, one 8-byte store into each of hi and lo; each
     // 8-lane group reads and writes whole 128-byte rows (no bank conflicts).
     // A lane's rows r = 2 (cw + 4 j) + l / 16 all have the same r % 8, so its
     // swizzled chunk positions are fixed and the rows 1 KB apart.
@@ -1728,18 +1737,18 @@ __global__ void __launch_bounds__(kGemmThreadsF, 1)
             v[j] = *reinterpret_cast<const float4*>(L + (j0 + j) * kRowStep);
 #pragma unroll
           for (int j = 0; j < kConvRows; ++j) {
-            const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[j].x, v[j].y);
-            const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[j].z, v[j].w);
-            const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[j].x - __low2float(h01),
-                                                             v[j].y - __high2float(h01));
-            const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[j].z - __low2float(h23),
-                                                             v[j].w - __high2float(h23));
+            const uint32_t u0 = __float_as_uint(v[j].x), u1 = __float_as_uint(v[j].y);
+            const uint32_t u2 = __float_as_uint(v[j].z), u3 = __float_as_uint(v[j].w);
+            const float r0 = v[j].x - __uint_as_float(u0 & 0xffff0000u);
+            const float r1 = v[j].y - __uint_as_float(u1 & 0xffff0000u);
+            const float r2 = v[j].z - __uint_as_float(u2 & 0xffff0000u);
+            const float r3 = v[j].w - __uint_as_float(u3 & 0xffff0000u);
             uint8_t* d = C + (j0 + j) * kRowStep;
-            *reinterpret_cast<uint2*>(d) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
-                                                      *reinterpret_cast<const uint32_t*>(&h23));
+            *reinterpret_cast<uint2*>(d) = make_uint2(__byte_perm(u0, u1, 0x7632),
+                                                      __byte_perm(u2, u3, 0x7632));
             *reinterpret_cast<uint2*>(d + kCHalfBytes) =
-                make_uint2(*reinterpret_cast<const uint32_t*>(&l01),
-                           *reinterpret_cast<const uint32_t*>(&l23));
+                make_uint2(__byte_perm(__float_as_uint(r0), __float_as_uint(r1), 0x7632),
+                           __byte_perm(__float_as_uint(r2), __float_as_uint(r3), 0x7632));
           }
         }
         fence_proxy_async_smem();  // the tensor core reads these stores
