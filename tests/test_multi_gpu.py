@@ -36,7 +36,7 @@ def _rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
     return (torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b)).item()
 
 
-def _worker(rank: int, world: int, port: int, mode: str) -> None:
+def _worker(rank: int, world: int, port: int, mode: str, dtype_name: str = "bf16") -> None:
     import sys
     from datetime import timedelta
 
@@ -50,13 +50,14 @@ def _worker(rank: int, world: int, port: int, mode: str) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     torch.cuda.set_device(rank)
+    dt = torch.float32 if dtype_name == "fp32" else torch.bfloat16
     try:
         E, H, I, K = 8, 1024, 2048, 2
         tp = world if mode == "tp" else 1
         ep = world if mode == "ep" else 1
         comm = F.PeerComm(H)
-        full = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=5, tokens=1)
-        shard = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=5, tokens=1,
+        full = synthetic.make_layer(E, H, I, K, dtype=dt, seed=5, tokens=1)
+        shard = synthetic.make_layer(E, H, I, K, dtype=dt, seed=5, tokens=1,
                                      tp_rank=rank if tp > 1 else 0, tp_size=tp,
                                      ep_rank=rank if ep > 1 else 0, ep_size=ep)
         gen = torch.Generator(device="cuda")
@@ -65,10 +66,11 @@ def _worker(rank: int, world: int, port: int, mode: str) -> None:
         # batches on the grouped path, whose combine step sums the ranks'
         # outputs (100 tokens: two all-reducing launches of <= 64 tokens),
         # and single tokens again
-        xs = [torch.randn(H, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(5)]
-        xs.append(torch.randn(6, H, generator=gen, device="cuda").to(torch.bfloat16))
-        xs.append(torch.randn(100, H, generator=gen, device="cuda").to(torch.bfloat16))
-        xs += [torch.randn(H, generator=gen, device="cuda").to(torch.bfloat16) for _ in range(2)]
+        # (fp32: batches of >= 3 tokens on the fp32 grouped path)
+        xs = [torch.randn(H, generator=gen, device="cuda").to(dt) for _ in range(5)]
+        xs.append(torch.randn(6, H, generator=gen, device="cuda").to(dt))
+        xs.append(torch.randn(100, H, generator=gen, device="cuda").to(dt))
+        xs += [torch.randn(H, generator=gen, device="cuda").to(dt) for _ in range(2)]
         outs = []
         for x in xs:
             out = F.fused_moe_allreduce(x, shard.gate_w, shard.weight_buf, E, H, shard.I, K, comm,
@@ -82,7 +84,7 @@ def _worker(rank: int, world: int, port: int, mode: str) -> None:
             else:
                 ref = F.batched_fused_moe(x, full.gate_w, full.weight_buf, E, H, I, K)
             err = _rel_l2(out, ref)
-            assert err <= REL_L2_TOL, f"rank {rank} {mode}: rel L2 {err:.3e}"
+            assert err <= REL_L2_TOL, f"rank {rank} {mode} {dtype_name}: rel L2 {err:.3e}"
         # bit-identical on every rank
         flat = torch.cat([o.reshape(-1) for o in outs]).cpu()
         gathered = [torch.empty_like(flat) for _ in range(world)]
@@ -94,13 +96,14 @@ def _worker(rank: int, world: int, port: int, mode: str) -> None:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("dtype_name", ["bf16", "fp32"])
 @pytest.mark.parametrize("mode", ["tp", "ep"])
-def test_fused_allreduce_matches_whole_layer(mode):
+def test_fused_allreduce_matches_whole_layer(mode, dtype_name):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(WORLD, _free_port(), mode), nprocs=WORLD, join=True)
+    mp.spawn(_worker, args=(WORLD, _free_port(), mode, dtype_name), nprocs=WORLD, join=True)
 
 
 def _worker_batched_ep(rank: int, world: int, port: int) -> None:
