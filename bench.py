@@ -104,6 +104,10 @@ def parse():
     ap.add_argument("--decode-steps", type=int, default=5)
     ap.add_argument("--only-sweep", action="store_true",
                     help="run only the batched-decode sweep (N = 1) and print its JSON line")
+    ap.add_argument("--profile-layer", default="",
+                    help="CONFIG:T or ExHxIxK:T — run that layer (in --dtype, router bias when "
+                         "top_k < E) three times eagerly on one GPU and exit: the case the "
+                         "profiles/ ncu captures use")
     return ap.parse_args()
 
 
@@ -981,8 +985,33 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def profile_layer(args):
+    """Three eager calls of one layer (one GPU), for an ncu capture of its kernels."""
+    from warp_route import functional as F
+    from warp_route import synthetic
+
+    cfg, T = args.profile_layer.split(":")
+    T = int(T)
+    E, H, I, K = SHAPES[cfg] if cfg in SHAPES else (int(v) for v in cfg.split("x"))
+    dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    L = synthetic.make_layer(E, H, I, K, dtype=dt, seed=200, tokens=T, router_bias=K < E)
+    for _ in range(3):
+        out = F.fused_moe_routed(L.x, L.gate_w, L.weight_buf, E, H, I, K,
+                                 router_bias=L.router_bias)[0]
+    torch.cuda.synchronize()
+    st = F._load_extension().workspace_status(L.x)
+    if st != 0:
+        raise SystemExit(f"profile layer: device status {st}")
+    print(json.dumps({"profile_layer": args.profile_layer, "dtype": args.dtype,
+                      "out_abs_mean": float(out.float().abs().mean())}), flush=True)
+
+
 def main():
     args = parse()
+    if args.profile_layer:
+        torch.cuda.set_device(0)
+        profile_layer(args)
+        return
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference_arm(args, world, rank)
