@@ -318,9 +318,31 @@ WR_DEVINL int4 down_row_tile(int i, int e, int nmaxB, int kcB, const int* costB,
   return make_int4(costB[e] + tn * kcB * wB[e][0], rowB[e], wt, 0);
 }
 
-// Run by one whole CTA.  s_ids: dynamic shared memory of 8 * TK bytes when
-// TK <= kBucketSmemIds (the ids, then the weights, are staged there).  The
-// ids and weights were written by other CTAs of this launch: read through L2.
+// Warp-wide inclusive prefix sum.
+WR_DEVINL int warp_incl_sum(int v, int lane) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += u;
+  }
+  return v;
+}
+
+constexpr int kBucketWarps = kRouterSegments;  // the routing CTA's warps
+
+// Run by one whole CTA of kBucketWarps warps.  s_ids: dynamic shared memory
+// of 8 * TK bytes when TK <= kBucketSmemIds (the ids, then the weights, are
+// staged there).  The ids and weights were written by other CTAs of this
+// launch: read through L2.
+//
+// Work is linear in the pairs: warp w takes a contiguous span of the (token,
+// k) pairs; pass 1 counts its pairs per expert (lanes of one expert found
+// with match.any), a scan over the warps gives each warp its first rank in
+// every expert, the metadata (per-expert bases, tile counts and cost
+// prefixes) is one warp's shuffle scans over the experts, and pass 2 gives
+// each pair its row: expert base + the warp's running rank + its rank among
+// the warp's lanes of that expert.  Rows of an expert are therefore in pair
+// order, i.e. ascending token order (a token picks an expert at most once).
 __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
   const int32_t* __restrict__ ids = b.ids;
   const float* __restrict__ w = b.w;
@@ -339,9 +361,12 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
   __shared__ int s_rowB[kMaxExperts];   // down cost of one H tile row of its token tiles
   __shared__ int s_wB[kMaxExperts][2];  // chunk cost: full token tiles, last token tile
   __shared__ int s_ntlB[kMaxExperts];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __shared__ int s_wcnt[kBucketWarps][kMaxExperts];  // per warp: pairs, then running rank
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool staged = TK <= kBucketSmemIds;
   for (int i = threadIdx.x; i < cnt_words; i += blockDim.x) tile_cnt[i] = 0u;
+  for (int i = threadIdx.x; i < kBucketWarps * kMaxExperts; i += blockDim.x)
+    (&s_wcnt[0][0])[i] = 0;
   float* s_w = reinterpret_cast<float*>(s_ids + TK);
   for (int i = threadIdx.x; i < TK; i += blockDim.x) {
     const int id = __ldcg(ids + i);
@@ -366,16 +391,33 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
   };
   const Src sid{staged ? s_ids : ids, staged};
   const SrcF sw{staged ? s_w : w, staged};
-  for (int e = warp; e < E; e += nw) {
-    int c = 0;
-    for (int j = 0; j < TK; j += 32) {
-      const bool m = j + lane < TK && sid[j + lane] == e + ep_first;
-      c += __popc(__ballot_sync(0xffffffffu, m));
-    }
-    if (lane == 0) s_cnt[e] = c;
+  // this warp's span of pairs, a multiple of 32
+  const int span = ((TK + kBucketWarps - 1) / kBucketWarps + 31) & ~31;
+  const int j0 = warp * span;
+  const int j1 = min(TK, j0 + span);
+  // pass 1: the span's pairs per local expert
+  for (int j = j0; j < j1; j += 32) {
+    const int i = j + lane;
+    const int e = i < j1 ? sid[i] - ep_first : -1;
+    const bool mine = e >= 0 && e < E;
+    const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
+    if (mine && lane == __ffs(peers) - 1) s_wcnt[warp][e] += __popc(peers);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  // per expert: each warp's first rank (exclusive scan over the warps), the total
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int v = 0; v < kBucketWarps; ++v) {
+      const int t = s_wcnt[v][e];
+      s_wcnt[v][e] = run;
+      run += t;
+    }
+    s_cnt[e] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // per-expert metadata: lane l takes experts l, l + 32 (E <= 64); bases,
+    // tile prefixes and cost prefixes are exclusive scans over the experts
     int* cnt = meta + kMetaHdr;
     int* base = cnt + E;
     int* ntlA = base + E;
@@ -384,66 +426,87 @@ __device__ void bucket_body(const BucketArgs& b, int* s_ids) {
     int* preB = preA + E + 1;
     int* costB = preB + E + 1;
     int* costA = costB + E + 1;
-    int b = 0, pa = 0, pb = 0, cb = 0, wmax = 1, ca = 0, wmaxA = 1;
-    for (int e = 0; e < E; ++e) {
-      const int n = s_cnt[e];
+    int cb_ = 0, cpa = 0, cpb = 0, ccb = 0, cca = 0, wmax = 1, wmaxA = 1;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const bool on = e < E;
+      const int n = on ? s_cnt[e] : 0;
       const int np = (n + 15) & ~15;
       const int na = (np + nmaxA - 1) / nmaxA;
       const int nb = (np + nmaxB - 1) / nmaxB;
-      cnt[e] = n;
-      base[e] = b;
-      s_base[e] = b;
-      ntlA[e] = na;
-      ntlB[e] = nb;
-      s_ntlB[e] = nb;
-      preA[e] = pa;
-      preB[e] = pb;
       const TileCost dc = tile_cost_of<false>(n, nb, nmaxB, kcB);
       const TileCost da = tile_cost_of<true>(n, na, nmaxA, kcA);
-      costA[e] = ca;
-      ca += mtA * (int)da.r;
-      if (na > 0) wmaxA = max(wmaxA, na > 1 ? da.wfull : da.wlast);
-      costB[e] = cb;
-      s_costB[e] = cb;
-      s_rowB[e] = (int)dc.r;
-      s_wB[e][0] = dc.wfull;
-      s_wB[e][1] = dc.wlast;
-      b += np;
-      pa += mtA * na;
-      pb += mtB * nb;
-      cb += mtB * (int)dc.r;
-      if (nb > 0) wmax = max(wmax, nb > 1 ? dc.wfull : dc.wlast);
+      const int vb = np, vpa = mtA * na, vpb = mtB * nb, vcb = mtB * (int)dc.r,
+                vca = mtA * (int)da.r;
+      const int ib = warp_incl_sum(vb, lane), ipa = warp_incl_sum(vpa, lane),
+                ipb = warp_incl_sum(vpb, lane), icb = warp_incl_sum(vcb, lane),
+                ica = warp_incl_sum(vca, lane);
+      if (on) {
+        const int xb = cb_ + ib - vb, xcb = ccb + icb - vcb;
+        cnt[e] = n;
+        base[e] = xb;
+        s_base[e] = xb;
+        ntlA[e] = na;
+        ntlB[e] = nb;
+        s_ntlB[e] = nb;
+        preA[e] = cpa + ipa - vpa;
+        preB[e] = cpb + ipb - vpb;
+        costA[e] = cca + ica - vca;
+        costB[e] = xcb;
+        s_costB[e] = xcb;
+        s_rowB[e] = (int)dc.r;
+        s_wB[e][0] = dc.wfull;
+        s_wB[e][1] = dc.wlast;
+        if (nb > 0) wmax = max(wmax, nb > 1 ? dc.wfull : dc.wlast);
+        if (na > 0) wmaxA = max(wmaxA, na > 1 ? da.wfull : da.wlast);
+      }
+      cb_ += __shfl_sync(0xffffffffu, ib, 31);
+      cpa += __shfl_sync(0xffffffffu, ipa, 31);
+      cpb += __shfl_sync(0xffffffffu, ipb, 31);
+      ccb += __shfl_sync(0xffffffffu, icb, 31);
+      cca += __shfl_sync(0xffffffffu, ica, 31);
     }
-    preA[E] = pa;
-    preB[E] = pb;
-    costB[E] = cb;
-    costA[E] = ca;
-    meta[0] = b;
-    meta[1] = pa;
-    meta[2] = pb;
-    meta[3] = cb;
-    meta[4] = wmax;
-    meta[5] = ca;
-    meta[6] = wmaxA;
+    wmax = __reduce_max_sync(0xffffffffu, wmax);
+    wmaxA = __reduce_max_sync(0xffffffffu, wmaxA);
+    if (lane == 0) {
+      preA[E] = cpa;
+      preB[E] = cpb;
+      costB[E] = ccb;
+      costA[E] = cca;
+      meta[0] = cb_;
+      meta[1] = cpa;
+      meta[2] = cpb;
+      meta[3] = ccb;
+      meta[4] = wmax;
+      meta[5] = cca;
+      meta[6] = wmaxA;
+    }
   }
   __syncthreads();
-  for (int e = warp; e < E; e += nw) {
-    const int b0 = s_base[e];
-    int run = b0;
-    for (int j = 0; j < TK; j += 32) {
-      const bool m = j + lane < TK && sid[j + lane] == e + ep_first;
-      const unsigned bal = __ballot_sync(0xffffffffu, m);
-      if (m) {
-        const int r = run + __popc(bal & ((1u << lane) - 1u));
-        slot[j + lane] = r;
-        row_tok[r] = (j + lane) / K;
-        row_tile[r] = down_row_tile(r - b0, e, nmaxB, kcB, s_costB, s_rowB, s_wB, s_ntlB);
-        row_w[r] = sw[j + lane];
-      }
-      run += __popc(bal);
+  // pass 2: each pair's row, in pair order within the warp's span
+  for (int j = j0; j < j1; j += 32) {
+    const int i = j + lane;
+    const int e = i < j1 ? sid[i] - ep_first : -1;
+    const bool mine = e >= 0 && e < E;
+    const unsigned peers = __match_any_sync(0xffffffffu, mine ? e : -1);
+    const int rank = mine ? s_wcnt[warp][e] + __popc(peers & ((1u << lane) - 1u)) : 0;
+    __syncwarp();  // every lane has read the running rank before its update
+    if (mine) {
+      const int b0 = s_base[e];
+      const int r = b0 + rank;
+      slot[i] = r;
+      row_tok[r] = i / K;
+      row_tile[r] = down_row_tile(rank, e, nmaxB, kcB, s_costB, s_rowB, s_wB, s_ntlB);
+      row_w[r] = sw[i];
+      if (lane == __ffs(peers) - 1) s_wcnt[warp][e] += __popc(peers);
     }
-    const int end = b0 + ((s_cnt[e] + 15) & ~15);
-    for (int r = run + lane; r < end; r += 32) {
+    __syncwarp();
+  }
+  // padding rows of each expert (up to a multiple of 16)
+  for (int e = warp; e < E; e += kBucketWarps) {
+    const int b0 = s_base[e], n = s_cnt[e];
+    const int end = b0 + ((n + 15) & ~15);
+    for (int r = b0 + n + lane; r < end; r += 32) {
       row_tok[r] = -1;
       row_tile[r] = down_row_tile(r - b0, e, nmaxB, kcB, s_costB, s_rowB, s_wB, s_ntlB);
       row_w[r] = 0.0f;
