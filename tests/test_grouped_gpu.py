@@ -85,6 +85,19 @@ def test_mixtral_batched_sweep_shape(T):
     assert torch.isfinite(out).all()
 
 
+def test_deepseek_shape_batch_256_tokens():
+    """64 experts, top_k 6, 1536 pairs: every bucketing warp's span holds
+    pairs of many experts (ranks carried across warps)."""
+    E, H, I, K = synthetic.SHAPES["deepseek"]
+    T = 256
+    L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=62, tokens=T,
+                             router_bias=True)
+    out, ids, w = _run(L, E, H, I, K)
+    _check_routing(ids, w, L, K)
+    _check_rows(out, L.x, L.gate_w, L.weight_buf, E, H, I, K, [0, 1, 100, 191, 192, 255],
+                L.router_bias)
+
+
 def test_deepseek_shape_many_idle_experts():
     E, H, I, K = synthetic.SHAPES["deepseek"]
     T = 24  # 144 (token, expert) pairs over 64 experts: many experts get none
@@ -270,11 +283,13 @@ def test_python_api_matches_c_abi():
     assert torch.equal(a, b)
 
 
-def test_many_pairs_bucket_reads_global():
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_many_pairs_bucket_reads_global(dtype):
     """More (token, expert) pairs than the bucket kernel stages in shared
-    memory (T * K > 5632): its passes read the routing from global memory."""
+    memory (T * K > 5632): its passes read the routing from global memory;
+    experts get hundreds of tokens (many token tiles each)."""
     E, H, I, K, T = 16, 256, 256, 8, 720  # 5760 pairs
-    L = synthetic.make_layer(E, H, I, K, dtype=torch.bfloat16, seed=61, tokens=T,
+    L = synthetic.make_layer(E, H, I, K, dtype=dtype, seed=61, tokens=T,
                              router_bias=True)
     out, ids, w = _run(L, E, H, I, K)
     _check_routing(ids, w, L, K)
