@@ -737,29 +737,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
     // activations are in shared memory before its rows come up instead of
     // each slot costing a grid-wide wait plus a copy in the consumers' path.
     // With AOFF == 0 the buffers overlap x, and the first window waits for
-    // the end of phase A (every consumer warp has published every slot).
-    // Both jobs are polled in one loop, so neither waits behind the other.
+    // the end of phase A in this CTA (every consumer warp has arrived on
+    // every slot's barrier; a warp arrives on the slots in order).
+    // Both jobs are polled in one loop, so neither waits behind the other;
+    // a window that can go is issued before a pending release, which may
+    // hold this thread while the SM's bulk copies drain.
     if (lane == 0) {
       const int NW = S * pl.nwin;
       const uint64_t pol = l2_policy_evict_last();
-      int pub = 0, win_j = 0;
+      int pub = 0, done = 0, win_j = 0;  // slots released / seen complete here
       uint64_t t_prog = globaltimer_ns();
       uint32_t spins = 0;
       bool ok = true;
       while (ok && (pub < S || win_j < NW)) {
         bool prog = false;
-        if (pub < S && mbar_test_wait(&slot_bar[pub], 0u)) {
-          fence_proxy_async_global();
-          red_release_gpu_add(&a.sync[kSyncSlot0 + pub], 1u);
-          ++pub;
-          prog = true;
-        }
+        while (done < S && mbar_test_wait(&slot_bar[done], 0u)) ++done;
         if (win_j < NW) {
           const int s = win_j / pl.nwin, win = win_j - s * pl.nwin;
           const int ab = win_j % pl.CB;
           const int use = win_j / pl.CB;
           bool ready = use > 0 ? mbar_test_wait(&act_empty[ab], (uint32_t)(use - 1) & 1u)
-                               : (pl.AOFF > 0 || pub == S);
+                               : (pl.AOFF > 0 || done == S);
           if (ready && win == 0) ready = ld_acquire_gpu(&a.sync[kSyncSlot0 + s]) >= (uint32_t)G;
           if (ready) {
             fence_proxy_async_global();  // the peers' activations, then async-proxy reads
@@ -776,6 +774,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
             ++win_j;
             prog = true;
           }
+        }
+        if (pub < done) {
+          fence_proxy_async_global();
+          red_release_gpu_add(&a.sync[kSyncSlot0 + pub], 1u);
+          ++pub;
+          prog = true;
         }
         if (prog) {
           t_prog = globaltimer_ns();
