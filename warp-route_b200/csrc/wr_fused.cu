@@ -1038,26 +1038,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_fused_stream(const FusedArgs a)
   if (a.comm.world > 0) {
     // ---- one-shot all-reduce: this CTA's rows of every rank ----
     // Each word of this rank's mailbox is polled until it carries this
-    // launch's epoch; the values are summed in source-rank order.
+    // launch's epoch; the values are summed in source-rank order.  Every
+    // source's word is loaded at once first (one memory latency instead of
+    // one per source), then any that is not there yet is polled alone.
     const uint32_t e = *s_epoch;
     const uint64_t t0 = globaltimer_ns();
     bool late = false;
     for (int idx = tid; idx < T * nb; idx += kThreads) {
       const int t = idx / nb;
       const int h = hb0 + (idx - t * nb);
+      const uint64_t* pb = a.comm.box[a.comm.rank] + ((size_t)(e & 1u) * kCommMaxTokens + t) * H + h;
+      const size_t qs = (size_t)2 * kCommMaxTokens * H;  // words between sources
+      uint64_t w[kMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q)
+        if (q < a.comm.world) w[q] = ld_relaxed_sys_u64(pb + q * qs);
       float o = 0.0f;
-      for (int q = 0; q < a.comm.world; ++q) {
-        const uint64_t* p =
-            a.comm.box[a.comm.rank] + (((size_t)q * 2 + (e & 1u)) * kCommMaxTokens + t) * H + h;
-        uint64_t w = ld_relaxed_sys_u64(p);
-        for (uint32_t spin = 1; (uint32_t)(w >> 32) != e && !late; ++spin) {
-          if ((spin & 63u) == 0 && globaltimer_ns() - t0 > a.comm.peer_wait_ns) {
-            atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_PEER);
-            late = true;
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) {
+        if (q < a.comm.world) {
+          for (uint32_t spin = 1; (uint32_t)(w[q] >> 32) != e && !late; ++spin) {
+            if ((spin & 63u) == 0 && globaltimer_ns() - t0 > a.comm.peer_wait_ns) {
+              atomicOr(&a.sync[kSyncStatus], DEV_TIMEOUT_PEER);
+              late = true;
+            }
+            w[q] = ld_relaxed_sys_u64(pb + q * qs);
           }
-          w = ld_relaxed_sys_u64(p);
+          o += __uint_as_float((uint32_t)w[q]);
         }
-        o += __uint_as_float((uint32_t)w);
       }
       const int64_t i = (int64_t)t * H + h;
       a.out[i] = residual_out(a.res, i, o);

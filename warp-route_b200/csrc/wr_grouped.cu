@@ -775,21 +775,33 @@ __global__ void __launch_bounds__(256) k_combine_ar(const float4* __restrict__ y
   bool late = false;
   for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += stride) {
     const int tl = it / H4, h4 = it - tl * H4;
+    // every source's four words loaded at once, then any missing one polled
+    // alone; summed in source-rank order
     float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < comm.world; ++q) {
-      const uint64_t* p = comm.box[comm.rank] +
-                          (((size_t)q * 2 + (ep & 1u)) * kCommMaxTokens + tl) * (size_t)H + 4 * h4;
+    const uint64_t* pb =
+        comm.box[comm.rank] + ((size_t)(ep & 1u) * kCommMaxTokens + tl) * (size_t)H + 4 * h4;
+    const size_t qs = (size_t)2 * kCommMaxTokens * H;  // words between sources
+    uint64_t wv[kMaxRanks][4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint64_t wv = ld_relaxed_sys_u64(p + c);
-        for (uint32_t spin = 1; (uint32_t)(wv >> 32) != ep && !late; ++spin) {
-          if ((spin & 63u) == 0 && globaltimer_ns() - tstart > comm.peer_wait_ns) {
-            atomicOr(ctl + 2, DEV_TIMEOUT_PEER);
-            late = true;
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (q < comm.world) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) wv[q][c] = ld_relaxed_sys_u64(pb + q * qs + c);
+      }
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {
+      if (q < comm.world) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          for (uint32_t spin = 1; (uint32_t)(wv[q][c] >> 32) != ep && !late; ++spin) {
+            if ((spin & 63u) == 0 && globaltimer_ns() - tstart > comm.peer_wait_ns) {
+              atomicOr(ctl + 2, DEV_TIMEOUT_PEER);
+              late = true;
+            }
+            wv[q][c] = ld_relaxed_sys_u64(pb + q * qs + c);
           }
-          wv = ld_relaxed_sys_u64(p + c);
+          o[c] += __uint_as_float((uint32_t)wv[q][c]);
         }
-        o[c] += __uint_as_float((uint32_t)wv);
       }
     }
     const int64_t i = (int64_t)(t0 + tl) * H + 4 * h4;
